@@ -1,0 +1,492 @@
+#!/usr/bin/env python
+"""Benchmark of the momentum selective scan hot path on B200.
+
+Workload (one "step"): the scan of a 4-layer MambaMomentum stack, forward and
+backward -- per layer B=32 sequences, L=1024, D=256 channels (d_model 128 x
+expand 2), N=16 states, with the block's softplus(delta + bias) and SiLU(z) gate
+fused into the kernels.  Metric: scan elements (B*L*D*N) per second, fwd+bwd,
+summed over all GPUs.  Multi-GPU runs are batch-sharded (weak scaling): every
+rank scans its own 32 sequences per layer; the data path has no collective.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+Rank 0 prints ONE JSON line.  ``--impl reference`` times the CPU restatement
+of the reference algorithm (oracle/, fp32 variant, all host threads) on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "scan elements/s (B·L·D·N) fwd+bwd and HBM GB/s vs peak at 1/2/4/8 B200"
+UNIT = "elements/s"
+
+# workload shape
+BSZ, SEQ, DIM, DST, LAYERS = 32, 1024, 256, 16, 4
+BETA, ALPHA = 0.6, 1.0
+ELEMS_PER_LAYER = BSZ * SEQ * DIM * DST
+
+CONFIG = {
+    "workload": "MambaMomentum 4-layer stack scan fwd+bwd (d_model 128, expand 2, d_state 16): "
+                "B=32 L=1024 D=256 N=16 per layer, softplus(delta+bias) and SiLU(z) gate fused",
+    "batch": BSZ, "seqlen": SEQ, "dim": DIM, "dstate": DST, "layers": LAYERS,
+    "beta": BETA, "alpha": ALPHA,
+    "l2": "inputs larger than L2: 4 layers x 138 MB of scan inputs per step",
+}
+
+
+def fwd_bytes(Bsz=BSZ, L=SEQ, D=DIM, N=DST):
+    """Algorithmic bytes of one forward launch: read x, delta, z, B, C, A, D, bias;
+    write out."""
+    return 4 * (4 * Bsz * L * D + 2 * Bsz * L * N + D * N + 2 * D)
+
+
+def bwd_bytes(Bsz=BSZ, L=SEQ, D=DIM, N=DST):
+    """Algorithmic bytes of one backward launch: read x, delta, z, dout, B, C, A, D,
+    bias; write dx, ddelta, dz, dB, dC, dA, dD, dbias."""
+    return 4 * (7 * Bsz * L * D + 4 * Bsz * L * N + 2 * D * N + 4 * D)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return float(pk["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic():
+    """DRAM bytes per backward launch from the committed ncu capture, if any."""
+    path = os.path.join(ROOT, "profiles", "mmscan_bwd_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "samples": len(sm),
+                "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+class Layer:
+    """Device-resident inputs, outputs and checkpoint workspace of one layer."""
+
+    def __init__(self, torch, lib, dev, gen, Bsz=BSZ):
+        f = torch.float32
+        self.Bsz = Bsz
+        self.x = torch.randn(Bsz, SEQ, DIM, device=dev, generator=gen)
+        self.delta = 0.5 * torch.randn(Bsz, SEQ, DIM, device=dev, generator=gen)  # raw dt_proj out
+        self.z = torch.randn(Bsz, SEQ, DIM, device=dev, generator=gen)
+        self.B = torch.randn(Bsz, SEQ, DST, device=dev, generator=gen)
+        self.C = torch.randn(Bsz, SEQ, DST, device=dev, generator=gen)
+        self.A = -torch.arange(1, DST + 1, device=dev, dtype=f).repeat(DIM, 1)
+        self.D = torch.ones(DIM, device=dev)
+        dt = torch.exp(torch.rand(DIM, device=dev, generator=gen) * (math.log(0.1) - math.log(1e-3))
+                       + math.log(1e-3))
+        self.bias = dt + torch.log(-torch.expm1(-dt))          # inverse softplus, as the block
+        self.dout = torch.randn(Bsz, SEQ, DIM, device=dev, generator=gen)
+        self.out = torch.empty(Bsz, SEQ, DIM, device=dev)
+        self.ckpt = torch.empty(lib.mmb_mmscan_ckpt_floats(Bsz, SEQ, DIM, DST), device=dev)
+        self.dx = torch.empty_like(self.x)
+        self.ddelta = torch.empty_like(self.x)
+        self.dz = torch.empty_like(self.x)
+        self.dB = torch.empty_like(self.B)
+        self.dC = torch.empty_like(self.C)
+        self.dA = torch.empty_like(self.A)
+        self.dD = torch.empty_like(self.D)
+        self.dbias = torch.empty_like(self.D)
+
+
+def make_desc(_lib, Bsz):
+    d = _lib.MMScanDesc()
+    d.batch, d.seqlen, d.dim, d.dstate = Bsz, SEQ, DIM, DST
+    d.x_stride[:] = (SEQ * DIM, DIM)
+    d.delta_stride[:] = (SEQ * DIM, DIM)
+    d.z_stride[:] = (SEQ * DIM, DIM)
+    d.B_stride[:] = (SEQ * DST, DST)
+    d.C_stride[:] = (SEQ * DST, DST)
+    d.beta, d.alpha, d.delta_softplus = BETA, ALPHA, 1
+    return d
+
+
+def run_b200(args):
+    import torch
+    import torch.distributed as dist
+
+    from momentummamba_b200 import _lib
+    from momentummamba_b200.selective_scan import selective_scan_momentum_fn
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+    lib = _lib.load()
+    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
+    layers = [Layer(torch, lib, dev, gen) for _ in range(LAYERS)]
+    desc = make_desc(_lib, BSZ)
+    P = _lib.ptr
+
+    def fwd(ly, stream):
+        st = lib.mmb_mmscan_fwd(desc, P(ly.x), P(ly.delta), P(ly.A), P(ly.B), P(ly.C), P(ly.D),
+                                P(ly.z), P(ly.bias), P(ly.out), P(ly.ckpt), stream)
+        _lib.check(st, "fwd")
+
+    def bwd(ly, stream):
+        st = lib.mmb_mmscan_bwd(desc, P(ly.x), P(ly.delta), P(ly.A), P(ly.B), P(ly.C), P(ly.D),
+                                P(ly.z), P(ly.bias), P(ly.ckpt), P(ly.dout), P(ly.dx),
+                                P(ly.ddelta), P(ly.dA), P(ly.dB), P(ly.dC), P(ly.dD), P(ly.dz),
+                                P(ly.dbias), stream)
+        _lib.check(st, "bwd")
+
+    def step():
+        s = _lib.stream_of(layers[0].x)
+        for ly in layers:
+            fwd(ly, s)
+            bwd(ly, s)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+
+    # warm-up (also sets the kernels' shared-memory attributes before capture)
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+
+    launch = "eager"
+    graph = None
+    if not args.no_graph:
+        try:
+            graph = torch.cuda.CUDAGraph()
+            s = torch.cuda.Stream(device=dev)
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(graph, stream=s):
+                    step()
+            torch.cuda.current_stream().wait_stream(s)
+            graph.replay()
+            torch.cuda.synchronize()
+            launch = "cuda graph"
+        except Exception as e:  # capture unsupported: stay eager, say so
+            graph = None
+            launch = f"eager (graph capture failed: {type(e).__name__})"
+
+    run = graph.replay if graph is not None else step
+    for _ in range(args.warmup):
+        run()
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
+    barrier()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    total_elems = ELEMS_PER_LAYER * LAYERS * args.steps * world
+    value = total_elems / (ms / 1e3)
+
+    # per-kernel durations (CUDA events on the launching stream), for the roofline
+    ly = layers[0]
+    s = _lib.stream_of(ly.x)
+    cs = torch.cuda.current_stream()
+    reps = 20
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(2 * reps)]
+    for i in range(reps):
+        lyr = layers[i % LAYERS]
+        evs[2 * i][0].record(cs)
+        fwd(lyr, s)
+        evs[2 * i][1].record(cs)
+        evs[2 * i + 1][0].record(cs)
+        bwd(lyr, s)
+        evs[2 * i + 1][1].record(cs)
+    torch.cuda.synchronize()
+    t_fwd = statistics.mean(evs[2 * i][0].elapsed_time(evs[2 * i][1]) for i in range(reps))
+    t_bwd = statistics.mean(evs[2 * i + 1][0].elapsed_time(evs[2 * i + 1][1]) for i in range(reps))
+
+    # end to end through the public autograd API with host buffers
+    e2e = run_e2e(torch, selective_scan_momentum_fn, dev, layers, args)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(budget_s=args.cpu_budget)
+
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+
+    peak, peak_kind = load_peaks()
+    bwd_b = bwd_bytes()
+    fwd_b = fwd_bytes()
+    achieved = bwd_b / (t_bwd / 1e3) / 1e9
+    traffic = load_traffic()
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(CONFIG, parallelism=f"batch-sharded x{world} (no data-path collective)",
+                       launch=launch),
+        "roofline": {
+            "kernel": "mmscan_bwd_kernel<16>", "bound": "hbm", "achieved": achieved,
+            "peak": peak, "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s",
+            "frac": achieved / peak,
+            "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
+            "algorithmic_bytes": bwd_b, "ms_per_launch": t_bwd,
+        },
+        "kernels": {
+            "mmscan_fwd_kernel<16>": {"ms": t_fwd, "algorithmic_bytes": fwd_b,
+                                      "GB/s": fwd_b / (t_fwd / 1e3) / 1e9,
+                                      "frac": fwd_b / (t_fwd / 1e3) / 1e9 / peak},
+            "mmscan_bwd_kernel<16>": {"ms": t_bwd, "algorithmic_bytes": bwd_b,
+                                      "GB/s": achieved, "frac": achieved / peak},
+        },
+        "hbm_gbs_step": LAYERS * (fwd_b + bwd_b) * args.steps / (ms / 1e3) / 1e9,
+        "e2e": e2e,
+        "gpu_launches": 2 * LAYERS * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+    }
+    return line
+
+
+def run_e2e(torch, fn, dev, layers, args, steps=3):
+    """Same metric through selective_scan_momentum_fn + autograd, with inputs
+    copied in from pinned host memory and all outputs copied back every step."""
+    host_in, host_out = [], []
+    for ly in layers:
+        host_in.append({k: getattr(ly, k).cpu().pin_memory()
+                        for k in ("x", "delta", "z", "B", "C", "dout")})
+        host_out.append({k: torch.empty(getattr(ly, k).shape, pin_memory=True)
+                         for k in ("out", "dx", "ddelta", "dz", "dB", "dC", "dA", "dD", "dbias")})
+    A, D, bias = layers[0].A, layers[0].D, layers[0].bias
+    h2d = sum(t.numel() * 4 for t in host_in[0].values()) * LAYERS
+    d2h = sum(t.numel() * 4 for t in host_out[0].values()) * LAYERS
+
+    def one():
+        for hi, ho in zip(host_in, host_out):
+            d = {k: v.to(dev, non_blocking=True) for k, v in hi.items()}
+            ins = [d["x"].requires_grad_(True), d["delta"].requires_grad_(True),
+                   A.detach().requires_grad_(True), d["B"].requires_grad_(True),
+                   d["C"].requires_grad_(True), D.detach().requires_grad_(True),
+                   d["z"].requires_grad_(True), bias.detach().requires_grad_(True)]
+            y = fn(ins[0], ins[1], ins[2], ins[3], ins[4], ins[5], z=ins[6], delta_bias=ins[7],
+                   delta_softplus=True, beta=BETA, alpha=ALPHA)
+            gx, gd, gA, gB, gC, gD, gz, gb = torch.autograd.grad(y, ins, d["dout"])
+            for k, v in (("out", y), ("dx", gx), ("ddelta", gd), ("dz", gz), ("dB", gB),
+                         ("dC", gC), ("dA", gA), ("dD", gD), ("dbias", gb)):
+                ho[k].copy_(v.detach(), non_blocking=True)
+
+    one()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        one()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"value": ELEMS_PER_LAYER * LAYERS / (ms / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
+            "steps": steps, "api": "selective_scan_momentum_fn + torch.autograd.grad"}
+
+
+# ---------------------------------------------------------------------------
+# CPU (oracle restatement of the reference algorithm)
+# ---------------------------------------------------------------------------
+def cpu_inputs(np, nseq, seed=0):
+    rng = np.random.default_rng(seed)
+    f = np.float32
+    x = rng.standard_normal((nseq, SEQ, DIM), dtype=f)
+    delta = (0.5 * rng.standard_normal((nseq, SEQ, DIM))).astype(f)
+    z = rng.standard_normal((nseq, SEQ, DIM), dtype=f)
+    B = rng.standard_normal((nseq, SEQ, DST), dtype=f)
+    C = rng.standard_normal((nseq, SEQ, DST), dtype=f)
+    A = -np.tile(np.arange(1, DST + 1, dtype=f), (DIM, 1))
+    D = np.ones(DIM, f)
+    dt = np.exp(rng.uniform(math.log(1e-3), math.log(0.1), DIM))
+    bias = (dt + np.log(-np.expm1(-dt))).astype(f)
+    dout = rng.standard_normal((nseq, SEQ, DIM), dtype=f)
+    return x, delta, A, B, C, D, z, bias, dout
+
+
+def cpu_scan_layer(oracle, inp):
+    x, delta, A, B, C, D, z, bias, dout = inp
+    oracle.mmscan_fwd(x, delta, A, B, C, D, z, bias, True, BETA, ALPHA, prec="f32")
+    oracle.mmscan_bwd(x, delta, A, B, C, D, z, bias, True, BETA, ALPHA, dout, prec="f32")
+
+
+def cpu_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_baseline(budget_s=15.0):
+    """Time the fp32 oracle (the reference recurrence restated in C) on the host
+    cores: whole layers of 4 sequences each, repeated until ~budget_s."""
+    import numpy as np
+
+    import oracle
+    cores = cpu_threads()
+    oracle.set_num_threads(cores)
+    nseq = 4
+    inp = cpu_inputs(np, nseq)
+    cpu_scan_layer(oracle, inp)  # warm
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        cpu_scan_layer(oracle, inp)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s or n >= 64:
+            break
+    dt = time.perf_counter() - t0
+    elems = n * nseq * SEQ * DIM * DST
+    return {"value": elems / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} layer passes (fwd+bwd) of {nseq} of the {BSZ} sequences, "
+                      f"{dt:.1f} s of CPU time; fp32 oracle/scan_oracle.c, OpenMP"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return None
+    import numpy as np
+
+    import oracle
+    cores = cpu_threads()
+    oracle.set_num_threads(cores)
+    # size each step so that warm-up + steps take about a minute
+    probe = cpu_inputs(np, 1)
+    t0 = time.perf_counter()
+    cpu_scan_layer(oracle, probe)
+    t_seq = time.perf_counter() - t0
+    total = max(1, args.steps + args.warmup)
+    nseq = int(max(1, min(BSZ, round(60.0 / (total * max(t_seq, 1e-3))))))
+    inp = cpu_inputs(np, nseq)
+    for _ in range(args.warmup):
+        cpu_scan_layer(oracle, inp)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_scan_layer(oracle, inp)
+    dt = time.perf_counter() - t0
+    elems = args.steps * nseq * SEQ * DIM * DST
+    value = elems / dt
+    sample = (f"each step: one layer's scan fwd+bwd on {nseq} of the {BSZ} sequences "
+              f"({nseq * SEQ * DIM * DST} elements); fp32 oracle/scan_oracle.c, OpenMP")
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": dt * 1e3 / max(1, args.steps),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "impl": "reference",
+        "config": dict(CONFIG, parallelism="host cores (rank 0 only)"),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    line = run_reference(args) if args.impl == "reference" else run_b200(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,137 @@
+/*
+ * momentum_scan_b200 -- C ABI of the B200 (sm_100a) momentum selective scan and
+ * LinOSS 2x2 scan kernels.
+ *
+ * Conventions shared by every entry point:
+ *   - all tensors are fp32 device pointers owned by the caller; the library never
+ *     allocates device memory.  Workspaces (forward checkpoints, chunk carries)
+ *     are caller-owned too; their size comes from the matching *_floats query.
+ *   - strides are in elements; the innermost dimension is always unit-stride.
+ *   - every call is asynchronous on `stream` (a cudaStream_t) and returns an
+ *     mmb_status; nothing synchronises the device.
+ *   - outputs are fully overwritten (gradient outputs that are sums over batch
+ *     or channels are cleared on `stream` before they are accumulated).
+ *   - nullable pointers are marked; a NULL there means "input absent" (for
+ *     inputs) or "not wanted" (for outputs).
+ */
+#ifndef MOMENTUM_SCAN_B200_H
+#define MOMENTUM_SCAN_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum mmb_status {
+    MMB_OK = 0,
+    MMB_ERR_NULL = 1,        /* a required pointer is NULL */
+    MMB_ERR_SHAPE = 2,       /* a size or stride is out of range */
+    MMB_ERR_ALIGN = 3,       /* a pointer or stride breaks the stated alignment */
+    MMB_ERR_UNSUPPORTED = 4, /* e.g. d_state outside the compiled set */
+    MMB_ERR_WORKSPACE = 5,   /* workspace pointer missing */
+    MMB_ERR_LAUNCH = 6,      /* the CUDA launch failed */
+    MMB_ERR_TIMEOUT = 7      /* a bounded device-side wait gave up */
+};
+
+typedef struct CUstream_st* mmb_stream_t; /* identical to cudaStream_t */
+
+/* Human-readable text for a status code (static storage). */
+const char* mmb_status_string(int status);
+
+/* ABI revision of this header; bumped on any incompatible change. */
+int mmb_abi_version(void);
+
+/* =========================================================================
+ * Momentum selective scan (fused discretisation, scan, C-contraction, D skip,
+ * optional softplus(delta + bias) and optional SiLU(z) gate):
+ *
+ *   dt  = softplus(delta + delta_bias) if delta_softplus else delta
+ *   a   = exp(dt * A[d,n]);   u = alpha * dt * B[b,t,n] * x[b,t,d]
+ *   v_t = beta * v_{t-1} + u_t ;   h_t = a_t * h_{t-1} + v_t      (h, v start at 0)
+ *   y   = sum_n C[b,t,n] * h_t[n] + D[d] * x ;   out = y * silu(z) if z else y
+ *
+ * Replaces MambaMomentumBlock.selective_scan_momentum (mamba_momentum.py:256-323)
+ * -- and with it _cuda_momentum_scan_sequential / _specialized_momentum_pscan
+ * (:325-413) -- plus the block's delta softplus (:247) and gate (:227-229).
+ *
+ * Shapes: x, delta, z, out, dout, dx, ddelta, dz (batch, seqlen, dim);
+ *         A, dA (dim, dstate); B, C, dB, dC (batch, seqlen, dstate);
+ *         D, delta_bias, dD, ddelta_bias (dim).
+ * dstate must be 8, 16, 32 or 64 (callers pad other sizes with zero states).
+ * out, dout, dx, ddelta, dz, dB, dC are contiguous.  16-byte aligned pointers
+ * and strides that are multiples of 4 take the vector path; anything else works
+ * with 4-byte copies.
+ * ========================================================================= */
+typedef struct mmb_mmscan_desc {
+    int64_t batch, seqlen, dim, dstate;
+    int64_t x_stride[2];     /* (batch, seq) strides of x     */
+    int64_t delta_stride[2]; /* (batch, seq) strides of delta */
+    int64_t z_stride[2];     /* (batch, seq) strides of z     */
+    int64_t B_stride[2];     /* (batch, seq) strides of B     */
+    int64_t C_stride[2];     /* (batch, seq) strides of C     */
+    float beta, alpha;
+    int32_t delta_softplus;
+    int32_t reserved;
+} mmb_mmscan_desc;
+
+/* Floats of checkpoint workspace the forward writes for the backward
+ * (the (h, v) state every 8 steps): batch * ceil(seqlen/8) * dim * dstate * 2. */
+size_t mmb_mmscan_ckpt_floats(int64_t batch, int64_t seqlen, int64_t dim, int64_t dstate);
+
+/* Forward.  D, z, delta_bias nullable.  ckpt nullable (inference: no
+ * checkpoints); the backward needs the checkpoints of the same call. */
+int mmb_mmscan_fwd(const mmb_mmscan_desc* desc, const float* x, const float* delta,
+                   const float* A, const float* B, const float* C, const float* D,
+                   const float* z, const float* delta_bias, float* out, float* ckpt,
+                   mmb_stream_t stream);
+
+/* Backward.  Inputs as in the forward plus ckpt (required) and dout.
+ * Outputs dx, ddelta, dA, dB, dC are required; dD (when D given), dz (when z
+ * given) and ddelta_bias (when delta_bias given) are nullable. */
+int mmb_mmscan_bwd(const mmb_mmscan_desc* desc, const float* x, const float* delta,
+                   const float* A, const float* B, const float* C, const float* D,
+                   const float* z, const float* delta_bias, const float* ckpt,
+                   const float* dout, float* dx, float* ddelta, float* dA, float* dB,
+                   float* dC, float* dD, float* dz, float* ddelta_bias,
+                   mmb_stream_t stream);
+
+/* =========================================================================
+ * Row scan:  v_t = beta*v_{t-1} + u_t ;  h_t = a_t*h_{t-1} + v_t  over the rows
+ * of contiguous (rows, L) tensors (t unit-stride).
+ *   Replaces momentum_scan_kernel / launch_forward (momentum_scan_cuda.py:22-47,
+ *   :89-108, :175-178) and warp_mat2_scan_kernel (warp_momentum_scan_cuda.py:34-126).
+ * v_out nullable.
+ * ========================================================================= */
+int mmb_rows_fwd(int64_t rows, int64_t L, const float* a, float beta, const float* u,
+                 float* h, float* v_out, mmb_stream_t stream);
+
+/* Adjoint of mmb_rows_fwd given g = dL/dh:
+ *   gh_t = g_t + a_{t+1} gh_{t+1};  gv_t = gh_t + beta gv_{t+1};
+ *   du_t = gv_t;  da_t = gh_t h_{t-1} (0 at t = 0).
+ *   Replaces momentum_scan_backward_kernel / launch_backward
+ *   (momentum_scan_cuda.py:49-87, :110-133); the gradient of
+ *   warp_mat2_scan_backward_kernel (warp_momentum_scan_cuda.py:130-230) is
+ *   defined to be this one.  da, du nullable. */
+int mmb_rows_bwd(int64_t rows, int64_t L, const float* g, const float* a, float beta,
+                 const float* h, float* da, float* du, mmb_stream_t stream);
+
+/* =========================================================================
+ * Diagonal scan in the PScan layout: H_t = A_t H_{t-1} + X_t along dim 1 of
+ * (batch, L, M) tensors (M = D*N flattened, unit stride).
+ *   Replaces PScan.forward / PScan.pscan (pscan.py:45-100, :160-194).
+ * ========================================================================= */
+int mmb_pscan_fwd(int64_t batch, int64_t L, int64_t M, const float* A, const float* X,
+                  float* H, mmb_stream_t stream);
+
+/* Adjoint (pscan.py:197-232): gX_t = G_t + A_{t+1} gX_{t+1};
+ * gA_t = H_{t-1} gX_t (0 at t = 0).  dA, dX nullable. */
+int mmb_pscan_bwd(int64_t batch, int64_t L, int64_t M, const float* A, const float* H,
+                  const float* G, float* dA, float* dX, mmb_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOMENTUM_SCAN_B200_H */

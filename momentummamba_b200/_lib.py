@@ -1,0 +1,106 @@
+"""ctypes binding of the C ABI in include/momentum_scan_b200.h.
+
+The shared library is built in-tree (``python -m momentummamba_b200.build``) and
+loaded once per process.  There is no fallback: if the library is missing or a
+tensor is not on a CUDA device the call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+import torch
+
+from . import build as _build
+
+_c_i64 = ctypes.c_int64
+_c_f = ctypes.c_float
+_c_i32 = ctypes.c_int32
+_c_p = ctypes.c_void_p
+_c_size = ctypes.c_size_t
+
+_lock = threading.Lock()
+_lib = None
+
+
+class MMScanDesc(ctypes.Structure):
+    """mirror of struct mmb_mmscan_desc"""
+    _fields_ = [
+        ("batch", _c_i64), ("seqlen", _c_i64), ("dim", _c_i64), ("dstate", _c_i64),
+        ("x_stride", _c_i64 * 2), ("delta_stride", _c_i64 * 2), ("z_stride", _c_i64 * 2),
+        ("B_stride", _c_i64 * 2), ("C_stride", _c_i64 * 2),
+        ("beta", _c_f), ("alpha", _c_f), ("delta_softplus", _c_i32), ("reserved", _c_i32),
+    ]
+
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "mmb_status_string": (ctypes.c_char_p, [ctypes.c_int]),
+    "mmb_abi_version": (ctypes.c_int, []),
+    "mmb_mmscan_ckpt_floats": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
+    "mmb_mmscan_fwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 10 + [_c_p]),
+    "mmb_mmscan_bwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 18 + [_c_p]),
+    "mmb_rows_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p]),
+    "mmb_rows_bwd": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p]),
+    "mmb_pscan_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p]),
+    "mmb_pscan_bwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p, _c_p, _c_p]),
+}
+
+
+def lib_path() -> str:
+    return _build.LIB_PATH
+
+
+def load():
+    """Load (building first if the sources are newer) the C-ABI library."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is None:
+            path = _build.LIB_PATH
+            if _build.is_stale():
+                _build.build()
+            if not os.path.exists(path):
+                raise ImportError(f"momentummamba_b200: CUDA library not found at {path}")
+            lib = ctypes.CDLL(path)
+            for name, (res, args) in _SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+def check(status: int, what: str) -> None:
+    if status != 0:
+        msg = load().mmb_status_string(int(status)).decode()
+        raise RuntimeError(f"momentummamba_b200: {what} failed: {msg} (status {status})")
+
+
+def require_cuda(*tensors) -> None:
+    """Raise unless every given tensor lives on the same CUDA device."""
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("momentummamba_b200 kernels need CUDA tensors (no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError("momentummamba_b200: all tensors must be on one CUDA device")
+
+
+def ptr(t):
+    """Device pointer of a CUDA tensor, or None."""
+    if t is None:
+        return None
+    if not t.is_cuda:
+        raise RuntimeError("momentummamba_b200 kernels need CUDA tensors (no CPU path)")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def stream_of(t: torch.Tensor):
+    return ctypes.c_void_p(torch.cuda.current_stream(t.device).cuda_stream)

@@ -27,6 +27,10 @@ complex tensors).  What each fixture exercises:
                LinOSS_pytorch.LinOSSLayer forward on a (B, L, H) batch (vmap path)
   mlin_im / mlin_imex
                mamba_linoss.apply_linoss_vectorized(..., scan_algorithm='vectorized')
+  mm_state_dict.json
+               parameter names and shapes of the reference MambaMomentum
+               (d_model=128, n_layers=2, dt_rank=8): the module tree a drop-in
+               must reproduce to load the reference's checkpoints
 """
 import math
 import os
@@ -211,6 +215,17 @@ def gen_mlin(ref, disc, seed):
           dC_real=gr[3], dC_imag=gr[4], dx=dx, ddelta=gr[6])
 
 
+def gen_state_dict(ref):
+    import json
+    mm = ref["mamba_momentum"]
+    m = mm.MambaMomentum(mm.MambaMomentumConfig(d_model=128, n_layers=2, dt_rank=8))
+    keys = {k: list(v.shape) for k, v in m.state_dict().items()}
+    path = os.path.join(HERE, "mm_state_dict.json")
+    with open(path, "w") as f:
+        json.dump(keys, f, indent=0, sort_keys=True)
+    print("wrote", path)
+
+
 def main():
     refdir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
     sys.path.insert(0, refdir)
@@ -232,6 +247,7 @@ def main():
     gen_lin_layer(ref, "IMEX", seed=11)
     gen_mlin(ref, "IM", seed=12)
     gen_mlin(ref, "IMEX", seed=13)
+    gen_state_dict(ref)
 
 
 if __name__ == "__main__":
