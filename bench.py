@@ -190,8 +190,9 @@ def run_b200(args):
                                 device_id=dev)
     lib = _lib.load()
     gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    layers = [Layer(torch, lib, dev, gen) for _ in range(LAYERS)]
-    desc = make_desc(_lib, BSZ)
+    bsz = args.batch if args.kernels_only else BSZ
+    layers = [Layer(torch, lib, dev, gen, Bsz=bsz) for _ in range(LAYERS)]
+    desc = make_desc(_lib, bsz)
     P = _lib.ptr
 
     def fwd(ly, stream):
@@ -220,6 +221,13 @@ def run_b200(args):
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
+    if args.kernels_only:
+        for _ in range(args.steps):
+            step()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.destroy_process_group()
+        return None
 
     launch = "eager"
     graph = None
@@ -481,6 +489,10 @@ def main():
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--kernels-only", action="store_true",
+                    help="run warm-up and steps eagerly and exit (for profiler captures)")
+    ap.add_argument("--batch", type=int, default=BSZ,
+                    help="sequences per layer (profiling only; the benchmark line uses 32)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     line = run_reference(args) if args.impl == "reference" else run_b200(args)

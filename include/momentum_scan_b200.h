@@ -43,6 +43,10 @@ const char* mmb_status_string(int status);
 /* ABI revision of this header; bumped on any incompatible change. */
 int mmb_abi_version(void);
 
+/* Text of the last CUDA runtime error behind an MMB_ERR_LAUNCH on the calling
+ * thread (static storage), or "no CUDA error recorded". */
+const char* mmb_last_error(void);
+
 /* =========================================================================
  * Momentum selective scan (fused discretisation, scan, C-contraction, D skip,
  * optional softplus(delta + bias) and optional SiLU(z) gate):

@@ -38,6 +38,7 @@ class MMScanDesc(ctypes.Structure):
 _SIGNATURES = {
     "mmb_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "mmb_abi_version": (ctypes.c_int, []),
+    "mmb_last_error": (ctypes.c_char_p, []),
     "mmb_mmscan_ckpt_floats": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "mmb_mmscan_fwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 10 + [_c_p]),
     "mmb_mmscan_bwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 18 + [_c_p]),
@@ -75,7 +76,10 @@ def load():
 
 def check(status: int, what: str) -> None:
     if status != 0:
-        msg = load().mmb_status_string(int(status)).decode()
+        lib = load()
+        msg = lib.mmb_status_string(int(status)).decode()
+        if status == 6:  # MMB_ERR_LAUNCH: add the CUDA runtime's own text
+            msg += f" [{lib.mmb_last_error().decode()}]"
         raise RuntimeError(f"momentummamba_b200: {what} failed: {msg} (status {status})")
 
 

@@ -18,3 +18,12 @@ extern "C" const char* mmb_status_string(int status) {
 }
 
 extern "C" int mmb_abi_version(void) { return MMB_ABI_VERSION; }
+
+static thread_local cudaError_t g_last_cuda_error = cudaSuccess;
+
+void mmb_record_cuda_error(cudaError_t e) { g_last_cuda_error = e; }
+
+extern "C" const char* mmb_last_error(void) {
+    if (g_last_cuda_error == cudaSuccess) return "no CUDA error recorded";
+    return cudaGetErrorString(g_last_cuda_error);
+}

@@ -79,10 +79,79 @@ __device__ __forceinline__ float ex2(float x) {
     return y;
 }
 
-// torch.nn.functional.softplus with beta = 1, threshold = 20.
-__device__ __forceinline__ float softplus_f(float r) { return r > 20.f ? r : log1pf(expf(r)); }
+__device__ __forceinline__ float rcp_approx(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 
-__device__ __forceinline__ float sigmoid_f(float r) { return 1.f / (1.f + expf(-r)); }
+// torch.nn.functional.softplus (beta = 1): log(1 + e^r) = max(r, 0) + log1p(w),
+// w = e^{-|r|} in (0, 1].  log1p(w) = 2 atanh(s) with s = w / (2 + w) in
+// (0, 1/3]; the atanh series s + s^3/3 + ... + s^13/13 has a truncation error
+// below 2e-8 relative there.  Inputs above 20 come out as r to fp32 precision,
+// matching torch's threshold branch.  `wout` returns w for the derivative.
+__device__ __forceinline__ float softplus_w(float r, float& wout) {
+    const float w = ex2(-fabsf(r) * MMB_LOG2E);
+    const float s = w * rcp_approx(2.f + w);
+    const float s2 = s * s;
+    float q = 1.f / 13.f;
+    q = fmaf(q, s2, 1.f / 11.f);
+    q = fmaf(q, s2, 1.f / 9.f);
+    q = fmaf(q, s2, 1.f / 7.f);
+    q = fmaf(q, s2, 1.f / 5.f);
+    q = fmaf(q, s2, 1.f / 3.f);
+    q = fmaf(q, s2, 1.f);
+    wout = w;
+    return fmaxf(r, 0.f) + 2.f * s * q;
+}
+
+__device__ __forceinline__ float softplus_f(float r) {
+    float w;
+    return softplus_w(r, w);
+}
+
+// d softplus / dr = sigmoid(r), from w = e^{-|r|}.
+__device__ __forceinline__ float softplus_grad(float r) {
+    const float w = ex2(-fabsf(r) * MMB_LOG2E);
+    const float inv = rcp_approx(1.f + w);
+    return r >= 0.f ? inv : w * inv;
+}
+
+__device__ __forceinline__ float sigmoid_f(float r) {
+    return rcp_approx(1.f + ex2(-r * MMB_LOG2E));
+}
+
+// ---------------------------------------------------------------------------
+// packed fp32 pairs (sm_100 f32x2 pipes)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\tmov.b64 rc, {%6, %7};\n\t"
+        "fma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "mul.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+    float2 d;
+    asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+        "mov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
+        "add.rn.f32x2 rd, ra, rb;\n\tmov.b64 {%0, %1}, rd;\n\t}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 f2(float a) { return make_float2(a, a); }
 
 // ---------------------------------------------------------------------------
 // warp reductions
@@ -148,10 +217,15 @@ __device__ __forceinline__ void red_add_v4(float* gaddr, float a, float b, float
 
 }  // namespace mmb
 
+// Last CUDA error seen by this library on the calling thread (see mmb_last_error).
+void mmb_record_cuda_error(cudaError_t e);
+
 // Host-side launch-status helper shared by the C-ABI wrappers.
 static inline int mmb_launch_status() {
     const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? MMB_OK : MMB_ERR_LAUNCH;
+    if (e == cudaSuccess) return MMB_OK;
+    mmb_record_cuda_error(e);
+    return MMB_ERR_LAUNCH;
 }
 
 // Raise a kernel's dynamic shared-memory limit once per device (the attribute
@@ -160,12 +234,17 @@ static inline int mmb_launch_status() {
 template <typename Kernel>
 static inline int mmb_smem_attr(Kernel kernel, size_t bytes, int* done) {
     int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MMB_MAX_DEVICES)
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= MMB_MAX_DEVICES) {
+        mmb_record_cuda_error(e);
         return MMB_ERR_LAUNCH;
+    }
     if (!done[dev]) {
-        if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)bytes) != cudaSuccess)
+        e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+        if (e != cudaSuccess) {
+            mmb_record_cuda_error(e);
             return MMB_ERR_LAUNCH;
+        }
         done[dev] = 1;
     }
     return MMB_OK;
