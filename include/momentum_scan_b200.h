@@ -134,6 +134,61 @@ int mmb_pscan_fwd(int64_t batch, int64_t L, int64_t M, const float* A, const flo
 int mmb_pscan_bwd(int64_t batch, int64_t L, int64_t M, const float* A, const float* H,
                   const float* G, float* dA, float* dX, mmb_stream_t stream);
 
+/* =========================================================================
+ * 2x2 scan  x_t = M_t x_{t-1} + F_t  per (b, p) chain, x_{-1} = 0, with the
+ * running matrix product Mscan_t = M_t Mscan_{t-1} (Mscan_{-1} = I).
+ *   M, Mscan, dM, gMscan : (batch, L, 4P) = [M11 | M12 | M21 | M22] blocks of P
+ *   F, X, gX, dF         : (batch, L, 2P) = [F1 | F2] blocks of P; complex entries
+ *                          are interleaved (re, im) float pairs when complex_f = 1
+ * Replaces parallel_scan_batched_complex (mamba_linoss.py:336-415) with its
+ * binary operator (:561-605) -- and the 'optimized' / 'vmap' scans of the same
+ * signature (:418-558, :680-763) -- parallel_scan_batched (LinOSS_pytorch.py:53-132)
+ * and pscan_matrix_ultra (pscan_optimized.py:42-158, P = 1).
+ * Chunked three-pass scan; `work` is caller workspace of
+ * mmb_scan2_work_floats(batch, L, P, complex_f) floats (scratch, any contents).
+ * ========================================================================= */
+size_t mmb_scan2_work_floats(int64_t batch, int64_t L, int64_t P, int32_t complex_f);
+
+/* Forward.  Mscan nullable (not wanted). */
+int mmb_scan2_fwd(int64_t batch, int64_t L, int64_t P, int32_t complex_f, const float* M,
+                  const float* F, float* Mscan, float* X, float* work, mmb_stream_t stream);
+
+/* Adjoint:  lambda_t = gX_t + M_{t+1}^T lambda_{t+1};  dF_t = lambda_t;
+ * dM_t = sum over (re, im) of lambda_t x_{t-1}^T, plus Lambda_t Mscan_{t-1}^T for
+ * the running product (Lambda_t = gMscan_t + M_{t+1}^T Lambda_{t+1}).
+ * X is the forward output.  gX and gMscan nullable (absent gradients); Mscan
+ * (the forward's) is required when gMscan is given.  dM, dF required. */
+int mmb_scan2_bwd(int64_t batch, int64_t L, int64_t P, int32_t complex_f, const float* M,
+                  const float* X, const float* gX, const float* Mscan, const float* gMscan,
+                  float* dM, float* dF, float* work, mmb_stream_t stream);
+
+/* =========================================================================
+ * LinOSS layer scan with a time-invariant transition per oscillator p -- the
+ * scan inside apply_linoss_im_complex / apply_linoss_imex_complex
+ * (LinOSS_pytorch.py:153-239), batched:
+ *   IM   (disc 0): S = 1/(1 + s^2 A); M = [[1 - s^2 A S, -s A S], [s S, S]];
+ *                  F_t = (M11 s Bu_t, M21 s Bu_t)
+ *   IMEX (disc 1): M = [[1, -s A], [s, 1 - s^2 A]];  F_t = (s Bu_t, s^2 Bu_t)
+ *   x_t = M x_{t-1} + F_t ;  output x2_t (the second state component).
+ * A_diag, step, dA_diag, dstep : (P); s = step[p], A = A_diag[p].
+ * Bu, x2, dx2, dBu : (batch, L, P) complex, interleaved (re, im), 8-byte aligned.
+ * The GEMMs around it (Bu = B u, y = Re(C x2)) stay with cuBLAS.
+ * `work`: mmb_linoss_work_floats(batch, L, P) floats, 16-byte aligned.  The
+ * forward leaves (x1, x2) checkpoints there; the backward needs the work buffer
+ * of its forward unchanged.
+ * ========================================================================= */
+size_t mmb_linoss_work_floats(int64_t batch, int64_t L, int64_t P);
+
+int mmb_linoss_fwd(int32_t disc, int64_t batch, int64_t L, int64_t P, const float* A_diag,
+                   const float* step, const float* Bu, float* x2, float* work,
+                   mmb_stream_t stream);
+
+/* Adjoint given dx2: writes dBu and, when non-NULL, dA_diag and dstep (the
+ * sums over batch and time of the transition's and input scale's gradients). */
+int mmb_linoss_bwd(int32_t disc, int64_t batch, int64_t L, int64_t P, const float* A_diag,
+                   const float* step, const float* Bu, const float* dx2, float* dBu,
+                   float* dA_diag, float* dstep, float* work, mmb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,740 @@
+// 2x2 linear scans (LinOSS), sm_100a.
+//
+//   x_t = M_t x_{t-1} + F_t ,   x = (x1, x2) per (b, p) chain, x_{-1} = 0,
+//
+// with M_t a real 2x2 matrix and F_t real or complex.  Every chain has length L;
+// to fill the GPU the sequence is cut into C chunks of T steps and scanned in
+// three passes, none of which waits on another CTA:
+//   1. chunk summaries   one thread per (b, chunk, p): the chunk's state from
+//                        zero and its matrix product
+//   2. carries           one thread per (b, p): compose the C summaries in order
+//   3. final pass        one thread per (b, chunk, p): rerun the chunk from its
+//                        carry and write the outputs
+// The backward is the same structure run in reverse on the adjoint
+//   lambda_t = gX_t + M_{t+1}^T lambda_{t+1},   dF_t = lambda_t,
+//   dM_t = sum over channels of lambda_t (x) x_{t-1}.
+// Threads of a warp take consecutive p, so for P >= 32 every load of a step is a
+// coalesced row.
+//
+// Two entry families:
+//   mmb_scan2_*    generic: M per (b, t, p) from memory, optional running product
+//                  Mscan (the "A_scan" the reference returns) and its gradient.
+//   mmb_linoss_*   LinOSS layer: M and F = (f1 Bu, f2 Bu) built in registers from
+//                  A_diag, step (IM or IMEX) and Bu; the forward also keeps
+//                  (x1, x2) every 8 steps so the backward can rebuild x_{t-1}.
+#include "mmb_common.cuh"
+
+namespace mmb {
+
+constexpr int S2_NT = 256;
+constexpr int S2_CK = 8;  // LinOSS checkpoint interval
+
+struct Mat2 {
+    float a, b, c, d;  // [[a, b], [c, d]]
+};
+__device__ __forceinline__ Mat2 mmul(const Mat2& x, const Mat2& y) {
+    return {x.a * y.a + x.b * y.c, x.a * y.b + x.b * y.d, x.c * y.a + x.d * y.c,
+            x.c * y.b + x.d * y.d};
+}
+__device__ __forceinline__ Mat2 mtrans(const Mat2& x) { return {x.a, x.c, x.b, x.d}; }
+__device__ __forceinline__ Mat2 mident() { return {1.f, 0.f, 0.f, 1.f}; }
+__device__ __forceinline__ void mvec(const Mat2& m, float& u, float& v) {
+    const float nu = m.a * u + m.b * v;
+    const float nv = m.c * u + m.d * v;
+    u = nu;
+    v = nv;
+}
+
+// Host-side chunking: enough (b, chunk, p) threads to fill the GPU, chunks of at
+// least 16 steps.
+static void s2_chunks(int64_t Bsz, int64_t L, int64_t P, int64_t& T, int64_t& C) {
+    const int64_t target = 148 * 2048;
+    int64_t chains = Bsz * P;
+    int64_t want = (target + chains - 1) / chains;
+    int64_t maxc = (L + 15) / 16;
+    if (want < 1) want = 1;
+    if (want > maxc) want = maxc;
+    T = (L + want - 1) / want;
+    C = (L + T - 1) / T;
+}
+
+// ---------------------------------------------------------------------------
+// generic scan: layout helpers
+// ---------------------------------------------------------------------------
+struct S2Params {
+    int64_t Bsz, L, P, T, C;
+    int nc;  // components per F entry: 1 real, 2 complex
+    const float *M, *F, *X, *gX, *Mscan_in, *gMs;
+    float *Mscan, *Xo, *dM, *dF;
+    float* work;
+};
+
+__device__ __forceinline__ int64_t m_off(const S2Params& p, int64_t b, int64_t t, int k, int64_t j) {
+    return ((b * p.L + t) * 4 + k) * p.P + j;
+}
+__device__ __forceinline__ int64_t f_off(const S2Params& p, int64_t b, int64_t t, int row,
+                                         int64_t j, int comp) {
+    return (((b * p.L + t) * 2 + row) * p.P + j) * p.nc + comp;
+}
+__device__ __forceinline__ Mat2 load_m(const S2Params& p, int64_t b, int64_t t, int64_t j) {
+    return {__ldg(p.M + m_off(p, b, t, 0, j)), __ldg(p.M + m_off(p, b, t, 1, j)),
+            __ldg(p.M + m_off(p, b, t, 2, j)), __ldg(p.M + m_off(p, b, t, 3, j))};
+}
+
+// work layout (floats), per (b, chunk, p) record:
+//   forward summary  : Mprod(4), x_loc(2*nc)
+//   forward carry    : Mpre(4), x_in(2*nc)
+constexpr int S2_REC = 8;  // floats per (b, chunk, p) record of each table (2*nc <= 4)
+
+// ---------------------------------------------------------------------------
+// generic forward
+// ---------------------------------------------------------------------------
+template <int NC, bool MSCAN>
+__global__ void __launch_bounds__(S2_NT) s2_fwd_summary(const S2Params p) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= p.Bsz * p.C * p.P) return;
+    const int64_t j = idx % p.P, bc = idx / p.P, c = bc % p.C, b = bc / p.C;
+    const int64_t t0 = c * p.T, t1 = min64(p.L, t0 + p.T);
+    float x1[NC], x2[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) x1[k] = x2[k] = 0.f;
+    Mat2 mp = mident();
+    for (int64_t t = t0; t < t1; ++t) {
+        const Mat2 m = load_m(p, b, t, j);
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const float f1 = __ldg(p.F + f_off(p, b, t, 0, j, k));
+            const float f2 = __ldg(p.F + f_off(p, b, t, 1, j, k));
+            const float n1 = m.a * x1[k] + m.b * x2[k] + f1;
+            const float n2 = m.c * x1[k] + m.d * x2[k] + f2;
+            x1[k] = n1;
+            x2[k] = n2;
+        }
+        mp = mmul(m, mp);
+    }
+    float* rec = p.work + idx * S2_REC;
+    rec[0] = mp.a; rec[1] = mp.b; rec[2] = mp.c; rec[3] = mp.d;
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        rec[4 + 2 * k] = x1[k];
+        rec[5 + 2 * k] = x2[k];
+    }
+}
+
+template <int NC, bool MSCAN>
+__global__ void __launch_bounds__(S2_NT) s2_fwd_carry(const S2Params p) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= p.Bsz * p.P) return;
+    const int64_t j = idx % p.P, b = idx / p.P;
+    float x1[NC], x2[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) x1[k] = x2[k] = 0.f;
+    Mat2 pre = mident();
+    const float* summ = p.work;
+    float* carry = p.work + p.Bsz * p.C * p.P * S2_REC;
+    for (int64_t c = 0; c < p.C; ++c) {
+        const int64_t r = (b * p.C + c) * p.P + j;
+        float* out = carry + r * S2_REC;
+        out[0] = pre.a; out[1] = pre.b; out[2] = pre.c; out[3] = pre.d;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            out[4 + 2 * k] = x1[k];
+            out[5 + 2 * k] = x2[k];
+        }
+        const float* s = summ + r * S2_REC;
+        const Mat2 mc = {s[0], s[1], s[2], s[3]};
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            mvec(mc, x1[k], x2[k]);
+            x1[k] += s[4 + 2 * k];
+            x2[k] += s[5 + 2 * k];
+        }
+        if (MSCAN) pre = mmul(mc, pre);
+    }
+}
+
+template <int NC, bool MSCAN>
+__global__ void __launch_bounds__(S2_NT) s2_fwd_final(const S2Params p) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= p.Bsz * p.C * p.P) return;
+    const int64_t j = idx % p.P, bc = idx / p.P, c = bc % p.C, b = bc / p.C;
+    const int64_t t0 = c * p.T, t1 = min64(p.L, t0 + p.T);
+    const float* in = p.work + p.Bsz * p.C * p.P * S2_REC + idx * S2_REC;
+    Mat2 mp = {in[0], in[1], in[2], in[3]};
+    float x1[NC], x2[NC];
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        x1[k] = in[4 + 2 * k];
+        x2[k] = in[5 + 2 * k];
+    }
+    for (int64_t t = t0; t < t1; ++t) {
+        const Mat2 m = load_m(p, b, t, j);
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            const float f1 = __ldg(p.F + f_off(p, b, t, 0, j, k));
+            const float f2 = __ldg(p.F + f_off(p, b, t, 1, j, k));
+            const float n1 = m.a * x1[k] + m.b * x2[k] + f1;
+            const float n2 = m.c * x1[k] + m.d * x2[k] + f2;
+            x1[k] = n1;
+            x2[k] = n2;
+            p.Xo[f_off(p, b, t, 0, j, k)] = n1;
+            p.Xo[f_off(p, b, t, 1, j, k)] = n2;
+        }
+        if (MSCAN) {
+            mp = mmul(m, mp);
+            p.Mscan[m_off(p, b, t, 0, j)] = mp.a;
+            p.Mscan[m_off(p, b, t, 1, j)] = mp.b;
+            p.Mscan[m_off(p, b, t, 2, j)] = mp.c;
+            p.Mscan[m_off(p, b, t, 3, j)] = mp.d;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// generic backward.  Vector channels: NC for x (re, im) and, with GMS, the two
+// columns of the adjoint of the running product.
+// work layout per (b, chunk, p): summary [lam(2*NV), Q(4), M_t0(4)], then mu(2*NV)
+// ---------------------------------------------------------------------------
+template <int NC, bool GMS>
+struct S2B {
+    static constexpr int NV = NC + (GMS ? 2 : 0);
+    static constexpr int SREC = 2 * NV + 8;
+    static constexpr int MREC = 2 * NV;
+};
+
+template <int NC, bool GMS>
+__device__ __forceinline__ void s2_gvec(const S2Params& p, int64_t b, int64_t t, int64_t j,
+                                        float (&g1)[S2B<NC, GMS>::NV],
+                                        float (&g2)[S2B<NC, GMS>::NV]) {
+#pragma unroll
+    for (int k = 0; k < NC; ++k) {
+        g1[k] = p.gX ? __ldg(p.gX + f_off(p, b, t, 0, j, k)) : 0.f;
+        g2[k] = p.gX ? __ldg(p.gX + f_off(p, b, t, 1, j, k)) : 0.f;
+    }
+    if (GMS) {
+        // column q of the running-product adjoint: (gMs[0][q], gMs[1][q])
+        g1[NC] = __ldg(p.gMs + m_off(p, b, t, 0, j));
+        g2[NC] = __ldg(p.gMs + m_off(p, b, t, 2, j));
+        g1[NC + 1] = __ldg(p.gMs + m_off(p, b, t, 1, j));
+        g2[NC + 1] = __ldg(p.gMs + m_off(p, b, t, 3, j));
+    }
+}
+
+template <int NC, bool GMS>
+__global__ void __launch_bounds__(S2_NT) s2_bwd_summary(const S2Params p) {
+    using Q = S2B<NC, GMS>;
+    constexpr int NV = Q::NV;
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= p.Bsz * p.C * p.P) return;
+    const int64_t j = idx % p.P, bc = idx / p.P, c = bc % p.C, b = bc / p.C;
+    const int64_t t0 = c * p.T, t1 = min64(p.L, t0 + p.T);
+    float l1[NV], l2[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) l1[k] = l2[k] = 0.f;
+    Mat2 q = mident();  // M_{t+1}^T ... M_{t1-1}^T
+    Mat2 mn = {0.f, 0.f, 0.f, 0.f};  // M_{t+1}; none past the chunk end
+    for (int64_t t = t1 - 1; t >= t0; --t) {
+        float g1[NV], g2[NV];
+        s2_gvec<NC, GMS>(p, b, t, j, g1, g2);
+        const Mat2 mt = mtrans(mn);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            float a = l1[k], bb = l2[k];
+            mvec(mt, a, bb);
+            l1[k] = a + g1[k];
+            l2[k] = bb + g2[k];
+        }
+        const Mat2 m = load_m(p, b, t, j);
+        if (t > t0) q = mmul(mtrans(m), q);
+        mn = m;
+    }
+    float* rec = p.work + idx * Q::SREC;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        rec[2 * k] = l1[k];
+        rec[2 * k + 1] = l2[k];
+    }
+    rec[2 * NV + 0] = q.a; rec[2 * NV + 1] = q.b; rec[2 * NV + 2] = q.c; rec[2 * NV + 3] = q.d;
+    rec[2 * NV + 4] = mn.a; rec[2 * NV + 5] = mn.b; rec[2 * NV + 6] = mn.c; rec[2 * NV + 7] = mn.d;
+}
+
+template <int NC, bool GMS>
+__global__ void __launch_bounds__(S2_NT) s2_bwd_carry(const S2Params p) {
+    using Q = S2B<NC, GMS>;
+    constexpr int NV = Q::NV;
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= p.Bsz * p.P) return;
+    const int64_t j = idx % p.P, b = idx / p.P;
+    float m1[NV], m2[NV];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) m1[k] = m2[k] = 0.f;
+    const float* summ = p.work;
+    float* mu = p.work + p.Bsz * p.C * p.P * Q::SREC;
+    for (int64_t c = p.C - 1; c >= 0; --c) {
+        const int64_t r = (b * p.C + c) * p.P + j;
+        float* out = mu + r * Q::MREC;
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            out[2 * k] = m1[k];
+            out[2 * k + 1] = m2[k];
+        }
+        const float* s = summ + r * Q::SREC;
+        const Mat2 q = {s[2 * NV], s[2 * NV + 1], s[2 * NV + 2], s[2 * NV + 3]};
+        const Mat2 mt0 = mtrans(Mat2{s[2 * NV + 4], s[2 * NV + 5], s[2 * NV + 6], s[2 * NV + 7]});
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            float a = m1[k], bb = m2[k];
+            mvec(q, a, bb);
+            a += s[2 * k];
+            bb += s[2 * k + 1];
+            mvec(mt0, a, bb);  // mu for the previous chunk
+            m1[k] = a;
+            m2[k] = bb;
+        }
+    }
+}
+
+template <int NC, bool GMS>
+__global__ void __launch_bounds__(S2_NT) s2_bwd_final(const S2Params p) {
+    using Q = S2B<NC, GMS>;
+    constexpr int NV = Q::NV;
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= p.Bsz * p.C * p.P) return;
+    const int64_t j = idx % p.P, bc = idx / p.P, c = bc % p.C, b = bc / p.C;
+    const int64_t t0 = c * p.T, t1 = min64(p.L, t0 + p.T);
+    const float* mu = p.work + p.Bsz * p.C * p.P * Q::SREC + idx * Q::MREC;
+    float l1[NV], l2[NV];  // holds M_{t+1}^T lambda_{t+1} before step t
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+        l1[k] = mu[2 * k];
+        l2[k] = mu[2 * k + 1];
+    }
+    for (int64_t t = t1 - 1; t >= t0; --t) {
+        float g1[NV], g2[NV];
+        s2_gvec<NC, GMS>(p, b, t, j, g1, g2);
+#pragma unroll
+        for (int k = 0; k < NV; ++k) {
+            l1[k] += g1[k];
+            l2[k] += g2[k];
+        }
+        // dF_t = lambda_t ; dM_t = sum over channels lambda_t (x) state_{t-1}
+        float d11 = 0.f, d12 = 0.f, d21 = 0.f, d22 = 0.f;
+#pragma unroll
+        for (int k = 0; k < NC; ++k) {
+            p.dF[f_off(p, b, t, 0, j, k)] = l1[k];
+            p.dF[f_off(p, b, t, 1, j, k)] = l2[k];
+            float s1 = 0.f, s2 = 0.f;
+            if (t > 0) {
+                s1 = __ldg(p.X + f_off(p, b, t - 1, 0, j, k));
+                s2 = __ldg(p.X + f_off(p, b, t - 1, 1, j, k));
+            }
+            d11 += l1[k] * s1; d12 += l1[k] * s2;
+            d21 += l2[k] * s1; d22 += l2[k] * s2;
+        }
+        if (GMS) {
+            Mat2 pc = mident();  // Mc_{t-1}; identity before the first step
+            if (t > 0)
+                pc = {__ldg(p.Mscan_in + m_off(p, b, t - 1, 0, j)),
+                      __ldg(p.Mscan_in + m_off(p, b, t - 1, 1, j)),
+                      __ldg(p.Mscan_in + m_off(p, b, t - 1, 2, j)),
+                      __ldg(p.Mscan_in + m_off(p, b, t - 1, 3, j))};
+            // column q of the adjoint pairs with column q of Mc_{t-1}
+            d11 += l1[NC] * pc.a + l1[NC + 1] * pc.b;
+            d12 += l1[NC] * pc.c + l1[NC + 1] * pc.d;
+            d21 += l2[NC] * pc.a + l2[NC + 1] * pc.b;
+            d22 += l2[NC] * pc.c + l2[NC + 1] * pc.d;
+        }
+        p.dM[m_off(p, b, t, 0, j)] = d11;
+        p.dM[m_off(p, b, t, 1, j)] = d12;
+        p.dM[m_off(p, b, t, 2, j)] = d21;
+        p.dM[m_off(p, b, t, 3, j)] = d22;
+        // carry M_t^T lambda_t to step t - 1
+        const Mat2 mt = mtrans(load_m(p, b, t, j));
+#pragma unroll
+        for (int k = 0; k < NV; ++k) mvec(mt, l1[k], l2[k]);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// LinOSS layer: time-invariant M per oscillator, F = (f1 Bu, f2 Bu), Bu complex
+// ---------------------------------------------------------------------------
+struct LinParams {
+    int64_t Bsz, L, P, T, C, K;  // K = checkpoints per chain (ceil(L / 8))
+    int disc;                    // 0 IM, 1 IMEX
+    const float *A, *step, *Bu, *dx2;
+    float *x2, *dBu, *dA, *dstep;
+    float* work;
+};
+
+struct LinCoef {
+    Mat2 m;
+    float f1, f2;
+};
+
+// IM:   S = 1/(1 + s^2 A); M = [[1 - s^2 A S, -s A S], [s S, S]]; f = (M11 s, M21 s)
+// IMEX: M = [[1, -s A], [s, 1 - s^2 A]]; f = (s, s^2)
+// (LinOSS_pytorch.py:164-178 and :209-222)
+__device__ __forceinline__ LinCoef lin_coef(int disc, float A, float s) {
+    LinCoef k;
+    if (disc == 0) {
+        const float S = 1.f / (1.f + s * s * A);
+        k.m = {1.f - s * s * A * S, -s * A * S, s * S, S};
+        k.f1 = k.m.a * s;
+        k.f2 = k.m.c * s;
+    } else {
+        k.m = {1.f, -s * A, s, 1.f - s * s * A};
+        k.f1 = s;
+        k.f2 = s * s;
+    }
+    return k;
+}
+
+// work layout (floats):
+//   ckpt  : Bsz * K * P * 4          (x1re, x1im, x2re, x2im every 8 steps)
+//   summ  : Bsz * C * P * 4          (chunk state from zero / chunk adjoint from zero)
+//   carry : Bsz * C * P * 4          (state entering / adjoint leaving each chunk)
+//   grad  : P * 8                    (dM11, dM12, dM21, dM22, df1, df2 accumulators)
+__device__ __forceinline__ float* lin_ckpt(const LinParams& q) { return q.work; }
+__device__ __forceinline__ float* lin_summ(const LinParams& q) {
+    return q.work + q.Bsz * q.K * q.P * 4;
+}
+__device__ __forceinline__ float* lin_carry(const LinParams& q) {
+    return lin_summ(q) + q.Bsz * q.C * q.P * 4;
+}
+__device__ __forceinline__ float* lin_grad(const LinParams& q) {
+    return lin_carry(q) + q.Bsz * q.C * q.P * 4;
+}
+
+__device__ __forceinline__ float2 ld_bu(const float* base, int64_t Bsz, int64_t L, int64_t P,
+                                        int64_t b, int64_t t, int64_t j) {
+    return __ldg(reinterpret_cast<const float2*>(base) + (b * L + t) * P + j);
+}
+
+__global__ void __launch_bounds__(S2_NT) lin_fwd_summary(const LinParams q) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= q.Bsz * q.C * q.P) return;
+    const int64_t j = idx % q.P, bc = idx / q.P, c = bc % q.C, b = bc / q.C;
+    const int64_t t0 = c * q.T, t1 = min64(q.L, t0 + q.T);
+    const LinCoef k = lin_coef(q.disc, q.A[j], q.step[j]);
+    float x1r = 0.f, x1i = 0.f, x2r = 0.f, x2i = 0.f;
+    for (int64_t t = t0; t < t1; ++t) {
+        const float2 u = ld_bu(q.Bu, q.Bsz, q.L, q.P, b, t, j);
+        const float n1r = k.m.a * x1r + k.m.b * x2r + k.f1 * u.x;
+        const float n1i = k.m.a * x1i + k.m.b * x2i + k.f1 * u.y;
+        const float n2r = k.m.c * x1r + k.m.d * x2r + k.f2 * u.x;
+        const float n2i = k.m.c * x1i + k.m.d * x2i + k.f2 * u.y;
+        x1r = n1r; x1i = n1i; x2r = n2r; x2i = n2i;
+    }
+    reinterpret_cast<float4*>(lin_summ(q))[idx] = make_float4(x1r, x1i, x2r, x2i);
+}
+
+__global__ void __launch_bounds__(S2_NT) lin_fwd_carry(const LinParams q) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= q.Bsz * q.P) return;
+    const int64_t j = idx % q.P, b = idx / q.P;
+    const LinCoef k = lin_coef(q.disc, q.A[j], q.step[j]);
+    Mat2 mT = mident();  // M^T, the transition over a full chunk
+    for (int64_t s = 0; s < q.T; ++s) mT = mmul(k.m, mT);
+    float x1r = 0.f, x1i = 0.f, x2r = 0.f, x2i = 0.f;
+    const float4* summ = reinterpret_cast<const float4*>(lin_summ(q));
+    float4* carry = reinterpret_cast<float4*>(lin_carry(q));
+    for (int64_t c = 0; c < q.C; ++c) {
+        const int64_t r = (b * q.C + c) * q.P + j;
+        carry[r] = make_float4(x1r, x1i, x2r, x2i);
+        const float4 s = summ[r];
+        mvec(mT, x1r, x2r);
+        mvec(mT, x1i, x2i);
+        x1r += s.x; x1i += s.y; x2r += s.z; x2i += s.w;
+    }
+}
+
+__global__ void __launch_bounds__(S2_NT) lin_fwd_final(const LinParams q) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= q.Bsz * q.C * q.P) return;
+    const int64_t j = idx % q.P, bc = idx / q.P, c = bc % q.C, b = bc / q.C;
+    const int64_t t0 = c * q.T, t1 = min64(q.L, t0 + q.T);
+    const LinCoef k = lin_coef(q.disc, q.A[j], q.step[j]);
+    const float4 in = reinterpret_cast<const float4*>(lin_carry(q))[idx];
+    float x1r = in.x, x1i = in.y, x2r = in.z, x2i = in.w;
+    float4* ck = reinterpret_cast<float4*>(lin_ckpt(q));
+    float2* xo = reinterpret_cast<float2*>(q.x2);
+    for (int64_t t = t0; t < t1; ++t) {
+        if (t % S2_CK == 0 && ck) ck[(b * q.K + t / S2_CK) * q.P + j] = make_float4(x1r, x1i, x2r, x2i);
+        const float2 u = ld_bu(q.Bu, q.Bsz, q.L, q.P, b, t, j);
+        const float n1r = k.m.a * x1r + k.m.b * x2r + k.f1 * u.x;
+        const float n1i = k.m.a * x1i + k.m.b * x2i + k.f1 * u.y;
+        const float n2r = k.m.c * x1r + k.m.d * x2r + k.f2 * u.x;
+        const float n2i = k.m.c * x1i + k.m.d * x2i + k.f2 * u.y;
+        x1r = n1r; x1i = n1i; x2r = n2r; x2i = n2i;
+        xo[(b * q.L + t) * q.P + j] = make_float2(x2r, x2i);
+    }
+}
+
+// backward: gX_t = (0, dx2_t);  lambda_t = gX_t + M^T lambda_{t+1}
+__global__ void __launch_bounds__(S2_NT) lin_bwd_summary(const LinParams q) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= q.Bsz * q.C * q.P) return;
+    const int64_t j = idx % q.P, bc = idx / q.P, c = bc % q.C, b = bc / q.C;
+    const int64_t t0 = c * q.T, t1 = min64(q.L, t0 + q.T);
+    const Mat2 mt = mtrans(lin_coef(q.disc, q.A[j], q.step[j]).m);
+    float l1r = 0.f, l1i = 0.f, l2r = 0.f, l2i = 0.f;
+    for (int64_t t = t1 - 1; t >= t0; --t) {
+        if (t < t1 - 1) {
+            mvec(mt, l1r, l2r);
+            mvec(mt, l1i, l2i);
+        }
+        const float2 g = ld_bu(q.dx2, q.Bsz, q.L, q.P, b, t, j);
+        l2r += g.x;
+        l2i += g.y;
+    }
+    reinterpret_cast<float4*>(lin_summ(q))[idx] = make_float4(l1r, l1i, l2r, l2i);
+}
+
+__global__ void __launch_bounds__(S2_NT) lin_bwd_carry(const LinParams q) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    if (idx >= q.Bsz * q.P) return;
+    const int64_t j = idx % q.P, b = idx / q.P;
+    const Mat2 mt = mtrans(lin_coef(q.disc, q.A[j], q.step[j]).m);
+    // mu_c = M^T lambda_{first step of chunk c+1}; lambda_{t0} = lam_loc + (M^T)^(T-1) mu_c.
+    // Only the last chunk can be shorter than T, and its mu is zero.
+    Mat2 pw = mident();
+    for (int64_t s = 1; s < q.T; ++s) pw = mmul(mt, pw);
+    float m1r = 0.f, m1i = 0.f, m2r = 0.f, m2i = 0.f;
+    const float4* summ = reinterpret_cast<const float4*>(lin_summ(q));
+    float4* carry = reinterpret_cast<float4*>(lin_carry(q));
+    for (int64_t c = q.C - 1; c >= 0; --c) {
+        const int64_t r = (b * q.C + c) * q.P + j;
+        carry[r] = make_float4(m1r, m1i, m2r, m2i);
+        mvec(pw, m1r, m2r);
+        mvec(pw, m1i, m2i);
+        const float4 l = summ[r];
+        m1r += l.x; m1i += l.y; m2r += l.z; m2i += l.w;
+        mvec(mt, m1r, m2r);
+        mvec(mt, m1i, m2i);
+    }
+}
+
+// Per chunk, 8-step windows in reverse: rebuild x_{t-1} from the forward
+// checkpoint, then run the adjoint; dBu_t = f1 lambda1_t + f2 lambda2_t;
+// dM += lambda_t x_{t-1}^T and (df1, df2) += (lambda1, lambda2) . Bu_t.
+__global__ void __launch_bounds__(S2_NT) lin_bwd_final(const LinParams q) {
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+    const bool active = idx < q.Bsz * q.C * q.P;
+    float g[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    int64_t j = 0;
+    if (active) {
+        j = idx % q.P;
+        const int64_t bc = idx / q.P, c = bc % q.C, b = bc / q.C;
+        const int64_t t0 = c * q.T, t1 = min64(q.L, t0 + q.T);
+        const LinCoef k = lin_coef(q.disc, q.A[j], q.step[j]);
+        const Mat2 mt = mtrans(k.m);
+        const float4 mu = reinterpret_cast<const float4*>(lin_carry(q))[idx];
+        float l1r = mu.x, l1i = mu.y, l2r = mu.z, l2i = mu.w;  // M^T lambda_{t+1}
+        const float4* ck = reinterpret_cast<const float4*>(lin_ckpt(q));
+        float2* dbu = reinterpret_cast<float2*>(q.dBu);
+        // windows of the checkpoint grid that overlap [t0, t1)
+        const int64_t wlast = (t1 - 1) / S2_CK, wfirst = t0 / S2_CK;
+        for (int64_t w = wlast; w >= wfirst; --w) {
+            const int64_t ws = w * S2_CK;
+            const float4 x0 = ck[(b * q.K + w) * q.P + j];
+            float xs[S2_CK + 1][4];
+            xs[0][0] = x0.x; xs[0][1] = x0.y; xs[0][2] = x0.z; xs[0][3] = x0.w;
+            float2 us[S2_CK];
+#pragma unroll
+            for (int s = 0; s < S2_CK; ++s) {
+                const int64_t t = ws + s;
+                const float2 u = t < q.L ? ld_bu(q.Bu, q.Bsz, q.L, q.P, b, t, j) : make_float2(0.f, 0.f);
+                us[s] = u;
+                xs[s + 1][0] = k.m.a * xs[s][0] + k.m.b * xs[s][2] + k.f1 * u.x;
+                xs[s + 1][1] = k.m.a * xs[s][1] + k.m.b * xs[s][3] + k.f1 * u.y;
+                xs[s + 1][2] = k.m.c * xs[s][0] + k.m.d * xs[s][2] + k.f2 * u.x;
+                xs[s + 1][3] = k.m.c * xs[s][1] + k.m.d * xs[s][3] + k.f2 * u.y;
+            }
+#pragma unroll
+            for (int s = S2_CK - 1; s >= 0; --s) {
+                const int64_t t = ws + s;
+                if (t < t0 || t >= t1) continue;
+                const float2 gx = ld_bu(q.dx2, q.Bsz, q.L, q.P, b, t, j);
+                const float a1r = l1r, a1i = l1i, a2r = l2r + gx.x, a2i = l2i + gx.y;  // lambda_t
+                dbu[(b * q.L + t) * q.P + j] =
+                    make_float2(k.f1 * a1r + k.f2 * a2r, k.f1 * a1i + k.f2 * a2i);
+                // state before step t (zero at t = 0: the checkpoint there is zero)
+                g[0] += a1r * xs[s][0] + a1i * xs[s][1];
+                g[1] += a1r * xs[s][2] + a1i * xs[s][3];
+                g[2] += a2r * xs[s][0] + a2i * xs[s][1];
+                g[3] += a2r * xs[s][2] + a2i * xs[s][3];
+                g[4] += a1r * us[s].x + a1i * us[s].y;
+                g[5] += a2r * us[s].x + a2i * us[s].y;
+                l1r = a1r; l1i = a1i; l2r = a2r; l2i = a2i;
+                mvec(mt, l1r, l2r);
+                mvec(mt, l1i, l2i);
+            }
+        }
+    }
+    // sum over (b, chunk) into per-oscillator accumulators; a warp spans
+    // consecutive p, so each thread adds its own
+    if (active) {
+        float* acc = lin_grad(q) + j * 8;
+#pragma unroll
+        for (int i = 0; i < 6; ++i) atomicAdd(acc + i, g[i]);
+    }
+}
+
+// chain rule from (dM, df1, df2) to (dA, dstep)
+__global__ void lin_bwd_params(const LinParams q) {
+    const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (j >= q.P) return;
+    const float* g = lin_grad(q) + j * 8;
+    const float A = q.A[j], s = q.step[j];
+    float dA, ds;
+    if (q.disc == 0) {
+        const float S = 1.f / (1.f + s * s * A);
+        const float S2 = S * S;
+        const float M11 = 1.f - s * s * A * S;
+        // partial derivatives of (M11, M12, M21, M22, f1, f2) by A and by s
+        const float pA[6] = {-s * s * S2, -s * S2, -s * s * s * S2, -s * s * S2, -s * s * s * S2,
+                             -s * s * s * s * S2};
+        const float pS[6] = {-2.f * s * A * S2, -A * S * (1.f - 2.f * s * s * A * S),
+                             S * (1.f - 2.f * s * s * A * S), -2.f * s * A * S2,
+                             M11 - 2.f * s * s * A * S2, 2.f * s * S - 2.f * s * s * s * A * S2};
+        dA = ds = 0.f;
+        for (int i = 0; i < 6; ++i) {
+            dA += g[i] * pA[i];
+            ds += g[i] * pS[i];
+        }
+    } else {
+        dA = g[1] * (-s) + g[3] * (-s * s);
+        ds = g[1] * (-A) + g[2] + g[3] * (-2.f * s * A) + g[4] + g[5] * 2.f * s;
+    }
+    if (q.dA) q.dA[j] = dA;
+    if (q.dstep) q.dstep[j] = ds;
+}
+
+static bool al16(const void* ptr) { return ptr == nullptr || ((uintptr_t)ptr & 15) == 0; }
+
+static unsigned s2_blocks(int64_t n) { return (unsigned)((n + S2_NT - 1) / S2_NT); }
+
+template <int NC, bool MS>
+static int s2_fwd_launch(const S2Params& p, cudaStream_t st) {
+    s2_fwd_summary<NC, MS><<<s2_blocks(p.Bsz * p.C * p.P), S2_NT, 0, st>>>(p);
+    s2_fwd_carry<NC, MS><<<s2_blocks(p.Bsz * p.P), S2_NT, 0, st>>>(p);
+    s2_fwd_final<NC, MS><<<s2_blocks(p.Bsz * p.C * p.P), S2_NT, 0, st>>>(p);
+    return mmb_launch_status();
+}
+
+template <int NC, bool GMS>
+static int s2_bwd_launch(const S2Params& p, cudaStream_t st) {
+    s2_bwd_summary<NC, GMS><<<s2_blocks(p.Bsz * p.C * p.P), S2_NT, 0, st>>>(p);
+    s2_bwd_carry<NC, GMS><<<s2_blocks(p.Bsz * p.P), S2_NT, 0, st>>>(p);
+    s2_bwd_final<NC, GMS><<<s2_blocks(p.Bsz * p.C * p.P), S2_NT, 0, st>>>(p);
+    return mmb_launch_status();
+}
+
+static size_t s2_work(int64_t Bsz, int64_t L, int64_t P, int nc) {
+    int64_t T, C;
+    s2_chunks(Bsz, L, P, T, C);
+    const int64_t nv = nc + 2;
+    const int64_t fwd = 2 * Bsz * C * P * S2_REC;
+    const int64_t bwd = Bsz * C * P * (2 * nv + 8 + 2 * nv);
+    return (size_t)(fwd > bwd ? fwd : bwd);
+}
+
+static void lin_dims(int64_t Bsz, int64_t L, int64_t P, LinParams& q) {
+    q.Bsz = Bsz;
+    q.L = L;
+    q.P = P;
+    s2_chunks(Bsz, L, P, q.T, q.C);
+    q.K = (L + S2_CK - 1) / S2_CK;
+}
+
+}  // namespace mmb
+
+using namespace mmb;
+
+extern "C" size_t mmb_scan2_work_floats(int64_t batch, int64_t L, int64_t P, int32_t complex_f) {
+    if (batch <= 0 || L <= 0 || P <= 0) return 0;
+    return s2_work(batch, L, P, complex_f ? 2 : 1);
+}
+
+extern "C" int mmb_scan2_fwd(int64_t batch, int64_t L, int64_t P, int32_t complex_f,
+                             const float* M, const float* F, float* Mscan, float* X, float* work,
+                             mmb_stream_t stream) {
+    if (!M || !F || !X) return MMB_ERR_NULL;
+    if (!work) return MMB_ERR_WORKSPACE;
+    if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
+    S2Params p{};
+    p.Bsz = batch; p.L = L; p.P = P; p.nc = complex_f ? 2 : 1;
+    s2_chunks(batch, L, P, p.T, p.C);
+    p.M = M; p.F = F; p.Mscan = Mscan; p.Xo = X; p.work = work;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (p.nc == 2) return Mscan ? s2_fwd_launch<2, true>(p, st) : s2_fwd_launch<2, false>(p, st);
+    return Mscan ? s2_fwd_launch<1, true>(p, st) : s2_fwd_launch<1, false>(p, st);
+}
+
+extern "C" int mmb_scan2_bwd(int64_t batch, int64_t L, int64_t P, int32_t complex_f,
+                             const float* M, const float* X, const float* gX, const float* Mscan,
+                             const float* gMscan, float* dM, float* dF, float* work,
+                             mmb_stream_t stream) {
+    if (!M || !X || !dM || !dF) return MMB_ERR_NULL;
+    if (gMscan && !Mscan) return MMB_ERR_NULL;
+    if (!work) return MMB_ERR_WORKSPACE;
+    if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
+    S2Params p{};
+    p.Bsz = batch; p.L = L; p.P = P; p.nc = complex_f ? 2 : 1;
+    s2_chunks(batch, L, P, p.T, p.C);
+    p.M = M; p.X = X; p.gX = gX; p.Mscan_in = Mscan; p.gMs = gMscan;
+    p.dM = dM; p.dF = dF; p.work = work;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (p.nc == 2) return gMscan ? s2_bwd_launch<2, true>(p, st) : s2_bwd_launch<2, false>(p, st);
+    return gMscan ? s2_bwd_launch<1, true>(p, st) : s2_bwd_launch<1, false>(p, st);
+}
+
+extern "C" size_t mmb_linoss_work_floats(int64_t batch, int64_t L, int64_t P) {
+    if (batch <= 0 || L <= 0 || P <= 0) return 0;
+    LinParams q{};
+    lin_dims(batch, L, P, q);
+    return (size_t)(q.Bsz * q.K * q.P * 4 + 2 * q.Bsz * q.C * q.P * 4 + q.P * 8);
+}
+
+extern "C" int mmb_linoss_fwd(int32_t disc, int64_t batch, int64_t L, int64_t P,
+                              const float* A_diag, const float* step, const float* Bu, float* x2,
+                              float* work, mmb_stream_t stream) {
+    if (!A_diag || !step || !Bu || !x2) return MMB_ERR_NULL;
+    if (!work) return MMB_ERR_WORKSPACE;
+    if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
+    if (disc != 0 && disc != 1) return MMB_ERR_UNSUPPORTED;
+    if (((uintptr_t)Bu & 7) || ((uintptr_t)x2 & 7) || !al16(work)) return MMB_ERR_ALIGN;
+    LinParams q{};
+    lin_dims(batch, L, P, q);
+    q.disc = disc; q.A = A_diag; q.step = step; q.Bu = Bu; q.x2 = x2; q.work = work;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    lin_fwd_summary<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
+    lin_fwd_carry<<<s2_blocks(q.Bsz * q.P), S2_NT, 0, st>>>(q);
+    lin_fwd_final<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
+    return mmb_launch_status();
+}
+
+extern "C" int mmb_linoss_bwd(int32_t disc, int64_t batch, int64_t L, int64_t P,
+                              const float* A_diag, const float* step, const float* Bu,
+                              const float* dx2, float* dBu, float* dA_diag, float* dstep,
+                              float* work, mmb_stream_t stream) {
+    if (!A_diag || !step || !Bu || !dx2 || !dBu) return MMB_ERR_NULL;
+    if (!work) return MMB_ERR_WORKSPACE;
+    if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
+    if (disc != 0 && disc != 1) return MMB_ERR_UNSUPPORTED;
+    if (((uintptr_t)Bu & 7) || ((uintptr_t)dx2 & 7) || ((uintptr_t)dBu & 7) || !al16(work))
+        return MMB_ERR_ALIGN;
+    LinParams q{};
+    lin_dims(batch, L, P, q);
+    q.disc = disc; q.A = A_diag; q.step = step; q.Bu = Bu; q.dx2 = dx2; q.dBu = dBu;
+    q.dA = dA_diag; q.dstep = dstep; q.work = work;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (cudaMemsetAsync(work + (size_t)(q.Bsz * q.K * q.P * 4 + 2 * q.Bsz * q.C * q.P * 4), 0,
+                        sizeof(float) * q.P * 8, st) != cudaSuccess)
+        return MMB_ERR_LAUNCH;
+    lin_bwd_summary<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
+    lin_bwd_carry<<<s2_blocks(q.Bsz * q.P), S2_NT, 0, st>>>(q);
+    lin_bwd_final<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
+    lin_bwd_params<<<(unsigned)((P + 127) / 128), 128, 0, st>>>(q);
+    return mmb_launch_status();
+}
