@@ -162,6 +162,34 @@ int mmb_scan2_bwd(int64_t batch, int64_t L, int64_t P, int32_t complex_f, const 
                   const float* X, const float* gX, const float* Mscan, const float* gMscan,
                   float* dM, float* dF, float* work, mmb_stream_t stream);
 
+/* -------------------------------------------------------------------------
+ * mmb_scan2_fwd without a workspace argument; no counterpart in the reference.
+ *
+ * For callers that cannot hand the library device memory at call time: an
+ * operator inside a host framework that owns all device memory and gives its
+ * plugins no way to allocate, or a latency-critical caller for whom a
+ * cudaMalloc (which can synchronise the whole device) is not acceptable.  The
+ * call allocates nothing; the caller still provides M, F, X (and Mscan) as in
+ * mmb_scan2_fwd, with the same meaning and layouts.
+ *
+ * The scratch is a fixed array of MMB_SCAN2_NOALLOC_SCRATCH_FLOATS floats
+ * (4 MiB) inside the library, resident on every GPU that loads the library
+ * until the process exits.  Limit: 16 * batch * P <= that size (at most 65536
+ * chains); larger problems return MMB_ERR_SHAPE.  When the chunking that
+ * mmb_scan2_fwd would use does not fit, fewer, longer chunks are used, so
+ * results agree with mmb_scan2_fwd to rounding.
+ * The first call on each device looks up the array's device address; make
+ * that first call before any stream capture on that device.  All calls on a
+ * device share the one array and it keeps the last call's contents (nothing in
+ * it needs to start at zero): calls that can overlap on the GPU race, so the
+ * caller must order them, e.g. on one stream.
+ * ------------------------------------------------------------------------- */
+#define MMB_SCAN2_NOALLOC_SCRATCH_FLOATS (1 << 20)
+
+int mmb_scan2_fwd_noalloc(int64_t batch, int64_t L, int64_t P, int32_t complex_f,
+                          const float* M, const float* F, float* Mscan, float* X,
+                          mmb_stream_t stream);
+
 /* =========================================================================
  * LinOSS layer scan with a time-invariant transition per oscillator p -- the
  * scan inside apply_linoss_im_complex / apply_linoss_imex_complex

@@ -22,6 +22,8 @@
 //   mmb_linoss_*   LinOSS layer: M and F = (f1 Bu, f2 Bu) built in registers from
 //                  A_diag, step (IM or IMEX) and Bu; the forward also keeps
 //                  (x1, x2) every 8 steps so the backward can rebuild x_{t-1}.
+#include <mutex>
+
 #include "mmb_common.cuh"
 
 namespace mmb {
@@ -737,4 +739,61 @@ extern "C" int mmb_linoss_bwd(int32_t disc, int64_t batch, int64_t L, int64_t P,
     lin_bwd_final<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
     lin_bwd_params<<<(unsigned)((P + 127) / 128), 128, 0, st>>>(q);
     return mmb_launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// No-allocation variant of mmb_scan2_fwd.  The chunk summaries and carries live
+// in a fixed device array of this file instead of a caller workspace; the
+// number of chunks is lowered until they fit.  Nothing in the array has to start
+// at zero: each call writes every record before it reads it.  Host code must not
+// pass the array's name to a kernel (on the host it only stands for the symbol);
+// its device address comes from cudaGetSymbolAddress, once per device.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) float s2_noalloc_scratch[MMB_SCAN2_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_scratch[MMB_MAX_DEVICES] = {};
+}  // namespace
+
+extern "C" int mmb_scan2_fwd_noalloc(int64_t batch, int64_t L, int64_t P, int32_t complex_f,
+                                     const float* M, const float* F, float* Mscan, float* X,
+                                     mmb_stream_t stream) {
+    if (!M || !F || !X) return MMB_ERR_NULL;
+    if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
+    // one summary and one carry record of S2_REC floats per (b, chunk, p)
+    const int64_t per_chunk = 2 * (int64_t)S2_REC * batch * P;
+    const int64_t max_chunks = (int64_t)MMB_SCAN2_NOALLOC_SCRATCH_FLOATS / per_chunk;
+    if (max_chunks < 1) return MMB_ERR_SHAPE;  // batch * P too large for the fixed scratch
+    S2Params p{};
+    p.Bsz = batch; p.L = L; p.P = P; p.nc = complex_f ? 2 : 1;
+    s2_chunks(batch, L, P, p.T, p.C);
+    if (p.C > max_chunks) {
+        p.T = (L + max_chunks - 1) / max_chunks;
+        p.C = (L + p.T - 1) / p.T;
+    }
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess || dev < 0 || dev >= MMB_MAX_DEVICES) {
+        mmb_record_cuda_error(e);
+        return MMB_ERR_LAUNCH;
+    }
+    float* scratch = nullptr;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!g_noalloc_scratch[dev]) {
+            float* ptr = nullptr;
+            e = cudaGetSymbolAddress(reinterpret_cast<void**>(&ptr), s2_noalloc_scratch);
+            if (e != cudaSuccess || ptr == nullptr) {
+                mmb_record_cuda_error(e);
+                return MMB_ERR_LAUNCH;
+            }
+            g_noalloc_scratch[dev] = ptr;
+        }
+        scratch = g_noalloc_scratch[dev];
+    }
+    p.M = M; p.F = F; p.Mscan = Mscan; p.Xo = X; p.work = scratch;
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    if (p.nc == 2) return Mscan ? s2_fwd_launch<2, true>(p, st) : s2_fwd_launch<2, false>(p, st);
+    return Mscan ? s2_fwd_launch<1, true>(p, st) : s2_fwd_launch<1, false>(p, st);
 }
