@@ -78,6 +78,23 @@ def load_traffic():
         return None
 
 
+def max_over_ranks(ms: float, world: int, device=None) -> float:
+    """Largest per-rank duration (the job's time); identity on one rank."""
+    if world <= 1:
+        return float(ms)
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([float(ms)], dtype=torch.float64,
+                     device=device if device is not None else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def job_rate(elems_per_rank: float, world: int, ms_job: float) -> float:
+    """Whole-job throughput: the units every rank processed over the slowest rank's time."""
+    return elems_per_rank * world / (ms_job / 1e3)
+
+
 # ---------------------------------------------------------------------------
 # clocks sampler
 # ---------------------------------------------------------------------------
@@ -267,13 +284,8 @@ def run_b200(args):
     torch.cuda.synchronize()
     barrier()
     clocks = sampler.stop() if sampler else None
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    total_elems = ELEMS_PER_LAYER * LAYERS * args.steps * world
-    value = total_elems / (ms / 1e3)
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    value = job_rate(ELEMS_PER_LAYER * LAYERS * args.steps, world, ms)
 
     # per-kernel durations (CUDA events on the launching stream), for the roofline
     ly = layers[0]
@@ -295,7 +307,12 @@ def run_b200(args):
     t_bwd = statistics.mean(evs[2 * i + 1][0].elapsed_time(evs[2 * i + 1][1]) for i in range(reps))
 
     # end to end through the public autograd API with host buffers
+    if world > 1:
+        dist.barrier()
     e2e = run_e2e(torch, selective_scan_momentum_fn, dev, layers, args)
+    e2e_ms = max_over_ranks(e2e["ms_per_step"], world, dev)
+    e2e["ms_per_step"] = e2e_ms
+    e2e["value"] = job_rate(ELEMS_PER_LAYER * LAYERS, world, e2e_ms)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
