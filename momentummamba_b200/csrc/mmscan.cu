@@ -1,22 +1,31 @@
 // Fused momentum selective scan for sm_100a: forward and backward.
 //
 // Work decomposition: one CTA of 128 threads owns one sequence b and a tile of
-// DT = 128 / (N/4) channels for the whole sequence; each thread owns one channel
-// d and 4 of its N states (h, v in registers), so the N/4 lanes of a channel
-// combine y = sum_n C h with two or three shuffles.  The sequence is streamed
-// through shared memory in chunks of T = 32 steps with double-buffered
-// cp.async (x, delta, z, B, C tiles; rows of the (B, L, D) tensors are
-// coalesced 16-byte copies).  Per-(t, d) work (softplus, alpha*dt*x, SiLU(z),
-// D*x) runs once per element of a tile in a pre-/post-pass, not once per state.
+// DT = 128 / G channels for the whole sequence, G = N / NP lanes per channel; a
+// thread owns one channel d and NP (2 or 4) of its N states, h and v in
+// registers, updated with packed fp32 pairs (sm_100 f32x2 FMA).  NP is picked
+// per call: 2 when the problem is so small that 4 states per thread would leave
+// the SMs under two warps each, else 4 (fewer cross-lane sums; measured faster
+// from B*D = 8192 channels up).  The sequence is streamed through shared memory in chunks of T = 32
+// steps with double-buffered cp.async (x, delta, z, B, C tiles; rows of the
+// (B, L, D) tensors are coalesced 16-byte copies).
 //
-// The forward stores (h, v) every CK = 8 steps as checkpoints.  The backward
-// walks the sequence in reverse, 8 steps at a time: it recomputes the 8-step
-// window forward from its checkpoint into registers (a_t and h_t), then runs the
-// adjoint recurrence backwards through the window:
+// Per 8-step block, each lane owns 8/G (t, d) items of its channel (at least
+// one): it computes softplus(delta + bias), alpha*dt*x and the SiLU(z) gate for
+// them once, the per-step scalars are shuffled to the channel's lanes, the
+// block's decay factors exp(dt*A) are issued before the recurrence, and the
+// channel's partial sums of y = C h are reduce-scattered so each lane finishes
+// its own items.
+//
+// The forward stores (h, v) every 8 steps as checkpoints.  The backward walks
+// the sequence in reverse, 8 steps at a time: it recomputes the window forward
+// from its checkpoint into registers (a_t and h_t), then runs the adjoint
+// backwards through it:
 //   gh_t = dy_t C_t + a_{t+1} gh_{t+1} ;  gv_t = gh_t + beta gv_{t+1}
-// d-sums for dB, dC are reduce-scattered across the warp, summed across the
-// CTA's warps in shared memory and added to global memory with vector
-// reductions; dA, dD, d(delta_bias) accumulate in registers over the sequence.
+// The n-sums (dx, ddelta, recomputed y) are reduce-scattered back to the
+// owning lanes; the d-sums of the dB | dC contributions go through a per-warp
+// shared window buffer and vector reductions to global memory; dA, dD and
+// d(delta_bias) accumulate in registers over the sequence.
 #include "mmb_common.cuh"
 
 namespace mmb {
@@ -24,33 +33,29 @@ namespace mmb {
 constexpr int MM_NT = 128;  // threads per CTA
 constexpr int MM_T = 32;    // steps per staged chunk
 constexpr int MM_CK = 8;    // checkpoint interval = steps per register block
-constexpr int MM_NPER = 4;  // states per thread
 constexpr unsigned FULL = 0xffffffffu;
+// cp.async pipeline depth in chunks (3 and 4 stages measured no faster: the
+// kernels are issue-latency bound, not load-latency bound)
+constexpr int MM_NS = 2;
 
-// How the backward sums the dB | dC contributions over channels:
-//   0: reduce-scatter across the warp's channels with shuffles every step, warp
-//      partials to shared memory, CTA sum + global vector reduction per chunk
-//   1: shared window buffer for the CTA, summed after every 8-step window
-//   2: per-warp window buffers, summed by each warp after every 8-step window
-#ifndef MMB_BWD_DSUM
-#define MMB_BWD_DSUM 2
-#endif
+__host__ __device__ constexpr int ilog2c(int v) { return v <= 1 ? 0 : 1 + ilog2c(v / 2); }
 
-template <int N>
+template <int N, int NP>
 struct MMCfg {
-    static constexpr int G = N / MM_NPER;  // lanes per channel
-    static constexpr int LOG2G = G == 2 ? 1 : G == 4 ? 2 : G == 8 ? 3 : G == 16 ? 4 : 0;
+    static constexpr int NP2 = NP / 2;                // packed pairs per thread
+    static constexpr int G = N / NP;                  // lanes per channel
+    static constexpr int LOG2G = ilog2c(G);
     static constexpr int LB = LOG2G < 3 ? LOG2G : 3;  // lane bits that split an 8-step block
-    static constexpr int IPL = MM_CK >> LB;           // per-(t, d) items a lane owns per block
+    static constexpr int IPL = MM_CK >> LB;           // (t, d) items a lane owns per block
     static constexpr int DT = MM_NT / G;              // channels per CTA
     static constexpr int DPW = 32 / G;                // channels per warp
     static constexpr int LOG2DPW = 5 - LOG2G;
-    // raw (T x DT) tile pitch: the 8/IPL rows x DPW channels a warp reads at once
-    // fall in distinct banks
-    static constexpr int RP = G == 16 ? DT + 4 : DT + DPW;
+    // raw (T x DT) tile pitch: the rows and channels a warp reads at once fall in
+    // distinct banks
+    static constexpr int RP = G >= 16 ? DT + 4 : DT + DPW;
     static constexpr int TR = MM_T * RP;
     static constexpr int TN = MM_T * N;
-    static_assert(N % MM_NPER == 0 && G >= 2 && G <= 16, "unsupported d_state");
+    static_assert((NP == 2 || NP == 4) && N % NP == 0 && G >= 2 && G <= 16, "unsupported shape");
 };
 
 // Lane (within its channel's group) that owns step s of an 8-step block: the
@@ -61,6 +66,27 @@ __host__ __device__ constexpr int block_owner(int s) {
     for (int b = 0; b < LB; ++b)
         if ((s >> (2 - b)) & 1) ng |= 1 << b;
     return ng;
+}
+
+// NP consecutive floats of shared memory as packed pairs.
+template <int NP>
+__device__ __forceinline__ void ld_pairs(const float* p, float2 (&o)[NP / 2]) {
+    if constexpr (NP == 4) {
+        const float4 q = *reinterpret_cast<const float4*>(p);
+        o[0] = make_float2(q.x, q.y);
+        o[1] = make_float2(q.z, q.w);
+    } else {
+        o[0] = *reinterpret_cast<const float2*>(p);
+    }
+}
+
+// sum_j c_j h_j over this thread's NP states
+template <int NP2>
+__device__ __forceinline__ float dot_pairs(const float2 (&c)[NP2], const float2 (&h)[NP2]) {
+    float2 acc = fmul2(c[0], h[0]);
+#pragma unroll
+    for (int j = 1; j < NP2; ++j) acc = ffma2(c[j], h[j], acc);
+    return acc.x + acc.y;
 }
 
 struct MMParams {
@@ -78,29 +104,48 @@ struct MMParams {
     float *dx, *ddelta, *dA, *dB, *dC, *dD, *dz, *ddbias;
 };
 
+// checkpoint record of (b, window k, channel d): 2N floats, lane ng's
+// [h(NP) | v(NP)] at ng * 2 * NP
 __device__ __forceinline__ int64_t ckpt_base(const MMParams& p, int64_t b, int64_t k, int64_t d,
                                              int N) {
     const int64_t K = (p.L + MM_CK - 1) / MM_CK;
     return ((b * K + k) * p.D + d) * (int64_t)(2 * N);
 }
 
+template <int NP>
+__device__ __forceinline__ void ckpt_store(float* dst, const float2 (&h)[NP / 2],
+                                           const float2 (&v)[NP / 2]) {
+    if constexpr (NP == 4) {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(h[0].x, h[0].y, h[1].x, h[1].y);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+    } else {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(h[0].x, h[0].y, v[0].x, v[0].y);
+    }
+}
+
+template <int NP>
+__device__ __forceinline__ void ckpt_load(const float* src, float2 (&h)[NP / 2],
+                                          float2 (&v)[NP / 2]) {
+    if constexpr (NP == 4) {
+        const float4 a = reinterpret_cast<const float4*>(src)[0];
+        const float4 c = reinterpret_cast<const float4*>(src)[1];
+        h[0] = make_float2(a.x, a.y); h[1] = make_float2(a.z, a.w);
+        v[0] = make_float2(c.x, c.y); v[1] = make_float2(c.z, c.w);
+    } else {
+        const float4 a = reinterpret_cast<const float4*>(src)[0];
+        h[0] = make_float2(a.x, a.y);
+        v[0] = make_float2(a.z, a.w);
+    }
+}
+
 // ---------------------------------------------------------------------------
 // forward
-//
-// Per 8-step block: each lane prepares its own IPL (t, d) items
-// (dt = softplus(delta + bias), alpha*dt*x); the block's 8 per-step scalars are
-// broadcast to the channel's lanes by shuffles and all 32 decay factors
-// exp(dt*A) of the block are issued before the recurrence, which then runs as
-// plain packed-FMA chains over the 8 steps.  The 8 partial sums of y are
-// reduce-scattered so each lane ends with the full y of its own items, and the
-// lane finishes those items (D skip, SiLU gate, store).  The next block's items
-// are prepared while the current block's exponentials are in flight.
 // ---------------------------------------------------------------------------
-template <int N, bool SOFTPLUS, bool HAS_Z>
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z>
 __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
-    using Cf = MMCfg<N>;
+    using Cf = MMCfg<N, NP>;
     constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, RP = Cf::RP, IPL = Cf::IPL, LB = Cf::LB;
-    constexpr int NBLK = T / MM_CK;
+    constexpr int NP2 = Cf::NP2, NBLK = T / MM_CK;
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     constexpr int STAGE = 3 * Cf::TR + 2 * Cf::TN;  // x | delta | z (T x RP), B | C (T x N)
@@ -117,17 +162,21 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
     const bool dvalid = d < p.D;
     const int dvalid_cols = (int)min64(DT, p.D - d0);
 
-    float2 A2a = f2(0.f), A2b = f2(0.f);
-    if (dvalid) {
-        const float* Ar = p.A + d * N + ng * MM_NPER;
-        A2a = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
-        A2b = make_float2(Ar[2] * MMB_LOG2E, Ar[3] * MMB_LOG2E);
+    float2 A2[NP2], h[NP2], v[NP2];
+#pragma unroll
+    for (int j = 0; j < NP2; ++j) {
+        A2[j] = f2(0.f);
+        h[j] = f2(0.f);
+        v[j] = f2(0.f);
+        if (dvalid) {
+            const float* Ar = p.A + d * N + ng * NP + 2 * j;
+            A2[j] = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
+        }
     }
     const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
     const float Dv = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
     const float alpha = p.alpha;
     const float2 beta2 = f2(p.beta);
-    float2 h01 = f2(0.f), h23 = f2(0.f), v01 = f2(0.f), v23 = f2(0.f);
     const int nchunks = (int)((p.L + T - 1) / T);
 
     auto stage = [&](int s, int c) {
@@ -159,14 +208,17 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
         }
     };
 
-    stage(0, 0);
-    cp_async_commit();
-    for (int c = 0; c < nchunks; ++c) {
-        if (c + 1 < nchunks) stage((c + 1) & 1, c + 1);
+#pragma unroll
+    for (int c = 0; c < MM_NS - 1; ++c) {
+        if (c < nchunks) stage(c, c);
         cp_async_commit();
-        cp_async_wait<1>();
+    }
+    for (int c = 0; c < nchunks; ++c) {
+        if (c + MM_NS - 1 < nchunks) stage((c + MM_NS - 1) % MM_NS, c + MM_NS - 1);
+        cp_async_commit();
+        cp_async_wait<MM_NS - 1>();
         __syncthreads();
-        const float* st = smem + (c & 1) * STAGE;
+        const float* st = smem + (c % MM_NS) * STAGE;
         const float* sx = st;
         const float* sdl = st + Cf::TR;
         const float* sz = st + 2 * Cf::TR;
@@ -186,12 +238,14 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
                 dts[s] = __shfl_sync(FULL, dti[s % IPL], src);
                 dtxs[s] = __shfl_sync(FULL, dtxi[s % IPL], src);
             }
-            float2 a[MM_CK][2];
+            float2 a[MM_CK][NP2];
 #pragma unroll
             for (int s = 0; s < MM_CK; ++s) {
-                const float2 e01 = fmul2(f2(dts[s]), A2a), e23 = fmul2(f2(dts[s]), A2b);
-                a[s][0] = make_float2(ex2(e01.x), ex2(e01.y));
-                a[s][1] = make_float2(ex2(e23.x), ex2(e23.y));
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    const float2 e = fmul2(f2(dts[s]), A2[j]);
+                    a[s][j] = make_float2(ex2(e.x), ex2(e.y));
+                }
             }
             // next block's items while the exponentials are in flight
             float nxi[IPL], ndti[IPL], ndtxi[IPL];
@@ -199,24 +253,21 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
             // checkpoint: state before the block's first step
             if (p.ckpt && dvalid && t0 + k * MM_CK < p.L) {
                 const int64_t kk = (t0 + k * MM_CK) / MM_CK;
-                float4* dst = reinterpret_cast<float4*>(p.ckpt + ckpt_base(p, b, kk, d, N) +
-                                                        ng * 2 * MM_NPER);
-                dst[0] = make_float4(h01.x, h01.y, h23.x, h23.y);
-                dst[1] = make_float4(v01.x, v01.y, v23.x, v23.y);
+                ckpt_store<NP>(p.ckpt + ckpt_base(p, b, kk, d, N) + ng * 2 * NP, h, v);
             }
             float y[MM_CK];
 #pragma unroll
             for (int s = 0; s < MM_CK; ++s) {
                 const int tt = k * MM_CK + s;
-                const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * N + ng * MM_NPER);
-                const float4 c4 = *reinterpret_cast<const float4*>(sC + tt * N + ng * MM_NPER);
-                v01 = ffma2(beta2, v01, fmul2(f2(dtxs[s]), make_float2(b4.x, b4.y)));
-                v23 = ffma2(beta2, v23, fmul2(f2(dtxs[s]), make_float2(b4.z, b4.w)));
-                h01 = ffma2(a[s][0], h01, v01);
-                h23 = ffma2(a[s][1], h23, v23);
-                float2 yy = fmul2(make_float2(c4.x, c4.y), h01);
-                yy = ffma2(make_float2(c4.z, c4.w), h23, yy);
-                y[s] = yy.x + yy.y;
+                float2 bq[NP2], cq[NP2];
+                ld_pairs<NP>(sB + tt * N + ng * NP, bq);
+                ld_pairs<NP>(sC + tt * N + ng * NP, cq);
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    v[j] = ffma2(beta2, v[j], fmul2(f2(dtxs[s]), bq[j]));
+                    h[j] = ffma2(a[s][j], h[j], v[j]);
+                }
+                y[s] = dot_pairs(cq, h);
             }
             reduce_scatter<MM_CK, 0, Cf::LOG2G>(y, lane);
             // finish this lane's items: D skip, gate, store
@@ -247,67 +298,59 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
 // ---------------------------------------------------------------------------
 // backward
 //
-// Chunks of 32 steps in reverse; inside a chunk, 8-step windows in reverse.  A
-// window replays the recurrence forward from its checkpoint keeping a_t and h_t
-// in registers, then runs the adjoint backwards through it.  Per-(t, d) work is
-// owned by one lane as in the forward, and the n-sums (dx, ddelta, the
-// recomputed y) are reduce-scattered back to the owning lanes.  The d-sums of
-// the dB | dC contributions go through a shared window buffer
-// [8 steps][DT channels][2N] (float4 columns XOR-swizzled by channel parity so
-// that each quarter-warp's stores hit distinct banks): after each window the
-// CTA sums the buffer over its DT channels and adds the 8 x 2N results to
-// global memory with vector reductions.
+// Chunks of 32 steps in reverse; inside a chunk, 8-step windows in reverse.
+// The d-sums of the dB | dC contributions go through a window buffer
+// [8 steps][DT channels][2N]: each thread stores its NP dB and NP dC terms as
+// units of NP floats (odd channels swap the dB and dC halves, so a warp's
+// stores hit distinct banks); after the window each warp sums its own DPW
+// channels' rows and adds the results to global memory with vector reductions.
 // ---------------------------------------------------------------------------
-template <int N, bool SOFTPLUS, bool HAS_Z>
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z>
 __global__ void __launch_bounds__(MM_NT) mmscan_bwd_kernel(const MMParams p) {
-    using Cf = MMCfg<N>;
+    using Cf = MMCfg<N, NP>;
     constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, RP = Cf::RP, IPL = Cf::IPL, LB = Cf::LB;
-    constexpr int TR = Cf::TR;
-    constexpr int WB = MM_CK * DT * 2 * N;  // window buffer floats
-    constexpr int NQ = 2 * N / 4;           // float4 columns per buffer row
-    constexpr int SWZ = NQ / 2;             // swizzle: odd channels swap the dB and dC halves
+    constexpr int NP2 = Cf::NP2, TR = Cf::TR, DPW = Cf::DPW;
+    constexpr int NQ = 2 * N / 4;  // float4 columns per window-buffer row
+    constexpr int SWZ = NQ / 2;    // float4 swizzle of odd channels (= G units of NP floats)
     extern __shared__ float4 smem4[];
     float* smem = reinterpret_cast<float*>(smem4);
     // stage s: [x | delta | z | dout] (T x RP), [B | C] (T x N)
     constexpr int STAGE = 4 * TR + 2 * Cf::TN;
-    float* wbuf = smem + 2 * STAGE;
+    float* wbuf = smem + MM_NS * STAGE;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ng = lane & (G - 1);
     const int lane_base = lane & ~(G - 1);
     const int ibase = rs_index<MM_CK, LB>(ng & ((1 << LB) - 1), 0);
     const bool item_lane = (ng >> LB) == 0;
-    const int dl = warp * Cf::DPW + (lane >> Cf::LOG2G);
+    const int dl = warp * DPW + (lane >> Cf::LOG2G);
     const int64_t b = blockIdx.y;
     const int64_t d0 = (int64_t)blockIdx.x * DT;
     const int64_t d = d0 + dl;
     const bool dvalid = d < p.D;
     const int dvalid_cols = (int)min64(DT, p.D - d0);
-    const int swz = (dl & 1) ? SWZ : 0;
+    const int swz_units = (dl & 1) ? G : 0;
 
-    float2 A2a = f2(0.f), A2b = f2(0.f);
-    if (dvalid) {
-        const float* Ar = p.A + d * N + ng * MM_NPER;
-        A2a = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
-        A2b = make_float2(Ar[2] * MMB_LOG2E, Ar[3] * MMB_LOG2E);
+    float2 A2[NP2], gh[NP2], gv[NP2], an[NP2], dA[NP2];
+#pragma unroll
+    for (int j = 0; j < NP2; ++j) {
+        A2[j] = gh[j] = gv[j] = an[j] = dA[j] = f2(0.f);
+        if (dvalid) {
+            const float* Ar = p.A + d * N + ng * NP + 2 * j;
+            A2[j] = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
+        }
     }
     const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
     const float Dv = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
     const float alpha = p.alpha;
     const float2 beta2 = f2(p.beta);
-    float2 gh01 = f2(0.f), gh23 = f2(0.f), gv01 = f2(0.f), gv23 = f2(0.f);
-    float2 an01 = f2(0.f), an23 = f2(0.f);  // a_{t+1}
-    float2 dA01 = f2(0.f), dA23 = f2(0.f);
     float accD = 0.f, accBias = 0.f;
     const int nchunks = (int)((p.L + T - 1) / T);
-    float4 nck_h = make_float4(0.f, 0.f, 0.f, 0.f), nck_v = nck_h;
-    auto ck_load = [&](int64_t k, float4& hq, float4& vq) {
-        if (dvalid) {
-            const float4* src = reinterpret_cast<const float4*>(
-                p.ckpt_in + ckpt_base(p, b, k, d, N) + ng * 2 * MM_NPER);
-            hq = src[0];
-            vq = src[1];
-        }
+    float2 nck_h[NP2], nck_v[NP2];  // checkpoint of the next window to process
+#pragma unroll
+    for (int j = 0; j < NP2; ++j) nck_h[j] = nck_v[j] = f2(0.f);
+    auto ck_load = [&](int64_t k) {
+        if (dvalid) ckpt_load<NP>(p.ckpt_in + ckpt_base(p, b, k, d, N) + ng * 2 * NP, nck_h, nck_v);
     };
 
     auto stage = [&](int s, int c) {
@@ -329,15 +372,18 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_kernel(const MMParams p) {
                                    p.cs[1], rv, N, p.vec, tid);
     };
 
-    stage(0, nchunks - 1);
-    cp_async_commit();
+#pragma unroll
+    for (int it = 0; it < MM_NS - 1; ++it) {
+        if (it < nchunks) stage(it, nchunks - 1 - it);
+        cp_async_commit();
+    }
     for (int it = 0; it < nchunks; ++it) {
         const int c = nchunks - 1 - it;
-        if (c > 0) stage((it + 1) & 1, c - 1);
+        if (it + MM_NS - 1 < nchunks) stage((it + MM_NS - 1) % MM_NS, c - (MM_NS - 1));
         cp_async_commit();
-        cp_async_wait<1>();
+        cp_async_wait<MM_NS - 1>();
         __syncthreads();
-        const float* st = smem + (it & 1) * STAGE;
+        const float* st = smem + (it % MM_NS) * STAGE;
         const float* sx = st;
         const float* sdl = st + TR;
         const float* sz = st + 2 * TR;
@@ -350,10 +396,14 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_kernel(const MMParams p) {
         for (int w = (Lc - 1) / MM_CK; w >= 0; --w) {
             const int w0 = w * MM_CK;
             // window checkpoint (loaded one window ahead)
-            if (it == 0 && w == (Lc - 1) / MM_CK) ck_load((t0 + w0) / MM_CK, nck_h, nck_v);
-            float2 h01 = make_float2(nck_h.x, nck_h.y), h23 = make_float2(nck_h.z, nck_h.w);
-            float2 v01 = make_float2(nck_v.x, nck_v.y), v23 = make_float2(nck_v.z, nck_v.w);
-            if (t0 + w0 > 0) ck_load((t0 + w0) / MM_CK - 1, nck_h, nck_v);
+            if (it == 0 && w == (Lc - 1) / MM_CK) ck_load((t0 + w0) / MM_CK);
+            float2 h[NP2], v[NP2];
+#pragma unroll
+            for (int j = 0; j < NP2; ++j) {
+                h[j] = nck_h[j];
+                v[j] = nck_v[j];
+            }
+            if (t0 + w0 > 0) ck_load((t0 + w0) / MM_CK - 1);
             // this lane's items: dt, alpha*dt*x, dy = dout*silu(z)
             float xi[IPL], ri[IPL], dti[IPL], dtxi[IPL], dyi[IPL];
 #pragma unroll
@@ -377,30 +427,33 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_kernel(const MMParams p) {
                 dts[s] = __shfl_sync(FULL, dti[s % IPL], src);
                 dtxs[s] = __shfl_sync(FULL, dtxi[s % IPL], src);
             }
-            float2 aa[MM_CK][2];
+            float2 aa[MM_CK][NP2];
 #pragma unroll
             for (int s = 0; s < MM_CK; ++s) {
-                const float2 e01 = fmul2(f2(dts[s]), A2a), e23 = fmul2(f2(dts[s]), A2b);
-                aa[s][0] = make_float2(ex2(e01.x), ex2(e01.y));
-                aa[s][1] = make_float2(ex2(e23.x), ex2(e23.y));
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    const float2 e = fmul2(f2(dts[s]), A2[j]);
+                    aa[s][j] = make_float2(ex2(e.x), ex2(e.y));
+                }
             }
             // forward replay of the window
-            float2 hh[MM_CK + 1][2];
+            float2 hh[MM_CK + 1][NP2];
             float yv[MM_CK];
-            hh[0][0] = h01; hh[0][1] = h23;
+#pragma unroll
+            for (int j = 0; j < NP2; ++j) hh[0][j] = h[j];
 #pragma unroll
             for (int s = 0; s < MM_CK; ++s) {
                 const int tt = w0 + s;
-                const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * N + ng * MM_NPER);
-                const float4 c4 = *reinterpret_cast<const float4*>(sC + tt * N + ng * MM_NPER);
-                v01 = ffma2(beta2, v01, fmul2(f2(dtxs[s]), make_float2(b4.x, b4.y)));
-                v23 = ffma2(beta2, v23, fmul2(f2(dtxs[s]), make_float2(b4.z, b4.w)));
-                h01 = ffma2(aa[s][0], h01, v01);
-                h23 = ffma2(aa[s][1], h23, v23);
-                hh[s + 1][0] = h01; hh[s + 1][1] = h23;
-                float2 yy = fmul2(make_float2(c4.x, c4.y), h01);
-                yy = ffma2(make_float2(c4.z, c4.w), h23, yy);
-                yv[s] = yy.x + yy.y;
+                float2 bq[NP2], cq[NP2];
+                ld_pairs<NP>(sB + tt * N + ng * NP, bq);
+                ld_pairs<NP>(sC + tt * N + ng * NP, cq);
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    v[j] = ffma2(beta2, v[j], fmul2(f2(dtxs[s]), bq[j]));
+                    h[j] = ffma2(aa[s][j], h[j], v[j]);
+                    hh[s + 1][j] = h[j];
+                }
+                yv[s] = dot_pairs(cq, h);
             }
             reduce_scatter<MM_CK, 0, Cf::LOG2G>(yv, lane);
             float dys[MM_CK];
@@ -415,53 +468,36 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_kernel(const MMParams p) {
 #pragma unroll
             for (int s = MM_CK - 1; s >= 0; --s) {
                 const int tt = w0 + s;
-                const float4 b4 = *reinterpret_cast<const float4*>(sB + tt * N + ng * MM_NPER);
-                const float4 c4 = *reinterpret_cast<const float4*>(sC + tt * N + ng * MM_NPER);
-                const float2 b01 = make_float2(b4.x, b4.y), b23 = make_float2(b4.z, b4.w);
+                float2 bq[NP2], cq[NP2];
+                ld_pairs<NP>(sB + tt * N + ng * NP, bq);
+                ld_pairs<NP>(sC + tt * N + ng * NP, cq);
                 const float2 dy2 = f2(dys[s]);
-                gh01 = ffma2(an01, gh01, fmul2(dy2, make_float2(c4.x, c4.y)));
-                gh23 = ffma2(an23, gh23, fmul2(dy2, make_float2(c4.z, c4.w)));
-                gv01 = ffma2(beta2, gv01, gh01);
-                gv23 = ffma2(beta2, gv23, gh23);
-                float2 sb = fmul2(gv01, b01);
-                sb = ffma2(gv23, b23, sb);
-                const float2 t01 = fmul2(fmul2(gh01, hh[s][0]), aa[s][0]);
-                const float2 t23 = fmul2(fmul2(gh23, hh[s][1]), aa[s][1]);
-                float2 sa = fmul2(t01, A2a);
-                sa = ffma2(t23, A2b, sa);
-                dA01 = ffma2(t01, f2(dts[s]), dA01);
-                dA23 = ffma2(t23, f2(dts[s]), dA23);
+                float2 sb = f2(0.f), sa = f2(0.f), pb[NP2], pc[NP2];
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    gh[j] = ffma2(an[j], gh[j], fmul2(dy2, cq[j]));
+                    gv[j] = ffma2(beta2, gv[j], gh[j]);
+                    sb = ffma2(gv[j], bq[j], sb);
+                    const float2 t2 = fmul2(fmul2(gh[j], hh[s][j]), aa[s][j]);
+                    sa = ffma2(t2, A2[j], sa);
+                    dA[j] = ffma2(t2, f2(dts[s]), dA[j]);
+                    pb[j] = fmul2(gv[j], f2(dtxs[s]));
+                    pc[j] = fmul2(dy2, hh[s + 1][j]);
+                    an[j] = aa[s][j];
+                }
                 sab[2 * s] = sa.x + sa.y;
                 sab[2 * s + 1] = sb.x + sb.y;
-                const float2 pb01 = fmul2(gv01, f2(dtxs[s])), pb23 = fmul2(gv23, f2(dtxs[s]));
-                const float2 pc01 = fmul2(dy2, hh[s + 1][0]), pc23 = fmul2(dy2, hh[s + 1][1]);
-                an01 = aa[s][0];
-                an23 = aa[s][1];
-#if MMB_BWD_DSUM == 0
-                {
-                    // d-sum over this warp's channels by reduce-scatter
-                    float vals[2 * MM_NPER] = {pb01.x, pb01.y, pb23.x, pb23.y,
-                                               pc01.x, pc01.y, pc23.x, pc23.y};
-                    reduce_scatter<2 * MM_NPER, Cf::LOG2G, Cf::LOG2DPW>(vals, lane);
-                    constexpr int KEEP =
-                        (2 * MM_NPER >> Cf::LOG2DPW) > 0 ? (2 * MM_NPER >> Cf::LOG2DPW) : 1;
-                    constexpr int USED_BITS = Cf::LOG2DPW < 3 ? Cf::LOG2DPW : 3;
-                    const int dbits = lane >> Cf::LOG2G;
-                    if ((dbits >> USED_BITS) == 0) {
-#pragma unroll
-                        for (int i = 0; i < KEEP; ++i) {
-                            const int idx = rs_index<2 * MM_NPER, Cf::LOG2DPW>(dbits, i);
-                            const int kind = idx / MM_NPER, n = ng * MM_NPER + idx % MM_NPER;
-                            wbuf[(warp * T + tt) * 2 * N + kind * N + n] = vals[i];
-                        }
-                    }
+                // dB | dC terms of (t, d, this lane's states) into the window buffer
+                float* rowp = wrow + s * DT * 2 * N;
+                if constexpr (NP == 4) {
+                    float4* r4 = reinterpret_cast<float4*>(rowp);
+                    r4[ng ^ swz_units] = make_float4(pb[0].x, pb[0].y, pb[1].x, pb[1].y);
+                    r4[(G + ng) ^ swz_units] = make_float4(pc[0].x, pc[0].y, pc[1].x, pc[1].y);
+                } else {
+                    float2* r2 = reinterpret_cast<float2*>(rowp);
+                    r2[ng ^ swz_units] = pb[0];
+                    r2[(G + ng) ^ swz_units] = pc[0];
                 }
-#else
-                // dB | dC contributions of (t, d, this lane's 4 states) into the window buffer
-                float4* rowq = reinterpret_cast<float4*>(wrow + s * DT * 2 * N);
-                rowq[(ng) ^ swz] = make_float4(pb01.x, pb01.y, pb23.x, pb23.y);
-                rowq[(G + ng) ^ swz] = make_float4(pc01.x, pc01.y, pc23.x, pc23.y);
-#endif
             }
             // n-sums back to the owning lanes: sab[2i], sab[2i + 1] = (SA, SB) of item i
             reduce_scatter<2 * MM_CK, 0, Cf::LOG2G>(sab, lane);
@@ -491,109 +527,54 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_kernel(const MMParams p) {
                     accBias += gdt;
                 }
             }
-#if MMB_BWD_DSUM == 1
-            __syncthreads();
-            // d-sum of the window buffer: (step, float4 column) pairs spread over the CTA
-            {
-                constexpr int ITEMS = MM_CK * NQ;                       // (step, column) pairs
-                constexpr int TPI = ITEMS >= MM_NT ? 1 : MM_NT / ITEMS;  // threads per pair
-                constexpr int IPT = ITEMS >= MM_NT ? ITEMS / MM_NT : 1;  // pairs per thread
-                constexpr int RPT = DT / TPI;                           // channel rows per thread
-                static_assert((TPI & (TPI - 1)) == 0 && DT % TPI == 0, "window reduction layout");
-#pragma unroll
-                for (int j = 0; j < IPT; ++j) {
-                    const int item = (tid / TPI) + j * (MM_NT / TPI), part = tid % TPI;
-                    const int s = item / NQ, q = item % NQ;
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-                    for (int r = 0; r < RPT; ++r) {
-                        const int row = part * RPT + r;
-                        const float4 v = reinterpret_cast<const float4*>(
-                            wbuf + (s * DT + row) * 2 * N)[q ^ ((row & 1) ? SWZ : 0)];
-                        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
-                    }
-#pragma unroll
-                    for (int m = 1; m < TPI; m <<= 1) {
-                        acc.x += __shfl_xor_sync(FULL, acc.x, m);
-                        acc.y += __shfl_xor_sync(FULL, acc.y, m);
-                        acc.z += __shfl_xor_sync(FULL, acc.z, m);
-                        acc.w += __shfl_xor_sync(FULL, acc.w, m);
-                    }
-                    const int64_t gt = t0 + w0 + s;
-                    if (part == 0 && gt < p.L) {
-                        const int col = q * 4;
-                        float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
-                        red_add_v4(dst, acc.x, acc.y, acc.z, acc.w);
-                    }
-                }
-            }
-            __syncthreads();
-#elif MMB_BWD_DSUM == 2
             __syncwarp();
-            // d-sum of this warp's part of the window buffer (its DPW channels)
+            // d-sum of this warp's rows of the window buffer (its DPW channels)
             {
                 constexpr int ITEMS = MM_CK * NQ;
                 constexpr int IPT = ITEMS >= 32 ? ITEMS / 32 : 1;
                 constexpr int TPI = ITEMS >= 32 ? 1 : 32 / ITEMS;
-                constexpr int RPT = Cf::DPW / TPI;
+                constexpr int RPT = DPW / TPI > 0 ? DPW / TPI : 1;
 #pragma unroll
                 for (int j = 0; j < IPT; ++j) {
                     const int item = (lane / TPI) + j * (32 / TPI), part = lane % TPI;
                     const int s = item / NQ, q = item % NQ;
-                    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+                    float2 acc01 = f2(0.f), acc23 = f2(0.f);
 #pragma unroll
                     for (int r = 0; r < RPT; ++r) {
-                        const int row = warp * Cf::DPW + part * RPT + r;
-                        const float4 v = reinterpret_cast<const float4*>(
+                        const int row = warp * DPW + part * RPT + r;
+                        const float4 vv = reinterpret_cast<const float4*>(
                             wbuf + (s * DT + row) * 2 * N)[q ^ ((row & 1) ? SWZ : 0)];
-                        acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+                        acc01 = fadd2(acc01, make_float2(vv.x, vv.y));
+                        acc23 = fadd2(acc23, make_float2(vv.z, vv.w));
                     }
 #pragma unroll
                     for (int m = 1; m < TPI; m <<= 1) {
-                        acc.x += __shfl_xor_sync(FULL, acc.x, m);
-                        acc.y += __shfl_xor_sync(FULL, acc.y, m);
-                        acc.z += __shfl_xor_sync(FULL, acc.z, m);
-                        acc.w += __shfl_xor_sync(FULL, acc.w, m);
+                        acc01.x += __shfl_xor_sync(FULL, acc01.x, m);
+                        acc01.y += __shfl_xor_sync(FULL, acc01.y, m);
+                        acc23.x += __shfl_xor_sync(FULL, acc23.x, m);
+                        acc23.y += __shfl_xor_sync(FULL, acc23.y, m);
                     }
                     const int64_t gt = t0 + w0 + s;
                     if (part == 0 && gt < p.L) {
                         const int col = q * 4;
                         float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
-                        red_add_v4(dst, acc.x, acc.y, acc.z, acc.w);
+                        red_add_v4(dst, acc01.x, acc01.y, acc23.x, acc23.y);
                     }
                 }
             }
             __syncwarp();
-#endif
         }
         __syncthreads();
-#if MMB_BWD_DSUM == 0
-        // dB | dC of this chunk: sum the warps' partials, add to global
-        for (int f = tid; f < T * 2 * N / 4; f += MM_NT) {
-            const int tt = (f * 4) / (2 * N), q = (f * 4) % (2 * N);
-            if (tt < Lc) {
-                float4 acc = *reinterpret_cast<const float4*>(wbuf + tt * 2 * N + q);
-#pragma unroll
-                for (int w2 = 1; w2 < 4; ++w2) {
-                    const float4 o =
-                        *reinterpret_cast<const float4*>(wbuf + (w2 * T + tt) * 2 * N + q);
-                    acc.x += o.x; acc.y += o.y; acc.z += o.z; acc.w += o.w;
-                }
-                float* dst = (q < N ? p.dB : p.dC) + (b * p.L + t0 + tt) * N + (q % N);
-                red_add_v4(dst, acc.x, acc.y, acc.z, acc.w);
-            }
-        }
-        __syncthreads();
-#endif
     }
 
-    // dA: this thread's 4 states of channel d, summed over its sequence
+    // dA: this thread's states of channel d, summed over its sequence
     if (dvalid) {
-        float* dst = p.dA + d * N + ng * MM_NPER;
-        atomicAdd(dst + 0, dA01.x);
-        atomicAdd(dst + 1, dA01.y);
-        atomicAdd(dst + 2, dA23.x);
-        atomicAdd(dst + 3, dA23.y);
+        float* dst = p.dA + d * N + ng * NP;
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) {
+            atomicAdd(dst + 2 * j, dA[j].x);
+            atomicAdd(dst + 2 * j + 1, dA[j].y);
+        }
     }
     // dD, dbias: sum the channel's lanes
     accD = lane_sum<0, Cf::LOG2G>(accD);
@@ -604,55 +585,69 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_kernel(const MMParams p) {
     }
 }
 
-template <int N>
+template <int N, int NP>
 size_t fwd_smem_bytes() {
-    using Cf = MMCfg<N>;
-    return sizeof(float) * (2 * (3 * Cf::TR + 2 * Cf::TN));
+    using Cf = MMCfg<N, NP>;
+    return sizeof(float) * (MM_NS * (3 * Cf::TR + 2 * Cf::TN));
 }
 
-template <int N>
+template <int N, int NP>
 size_t bwd_smem_bytes() {
-    using Cf = MMCfg<N>;
-    const size_t dsum = MMB_BWD_DSUM == 0 ? 4 * MM_T * 2 * N : MM_CK * Cf::DT * 2 * N;
-    return sizeof(float) * (2 * (4 * Cf::TR + 2 * Cf::TN) + dsum);
+    using Cf = MMCfg<N, NP>;
+    return sizeof(float) * (MM_NS * (4 * Cf::TR + 2 * Cf::TN) + MM_CK * Cf::DT * 2 * N);
 }
 
-template <int N, bool SP, bool Z>
+template <int N, int NP, bool SP, bool Z>
 int launch_fwd_t(const MMParams& p, cudaStream_t stream) {
-    using Cf = MMCfg<N>;
-    const size_t smem = fwd_smem_bytes<N>();
+    using Cf = MMCfg<N, NP>;
+    const size_t smem = fwd_smem_bytes<N, NP>();
     static int attr_done[MMB_MAX_DEVICES] = {};
-    const int st = mmb_smem_attr(mmscan_fwd_kernel<N, SP, Z>, smem, attr_done);
+    const int st = mmb_smem_attr(mmscan_fwd_kernel<N, NP, SP, Z>, smem, attr_done);
     if (st != MMB_OK) return st;
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
-    mmscan_fwd_kernel<N, SP, Z><<<grid, MM_NT, smem, stream>>>(p);
+    mmscan_fwd_kernel<N, NP, SP, Z><<<grid, MM_NT, smem, stream>>>(p);
     return mmb_launch_status();
 }
 
-template <int N, bool SP, bool Z>
+template <int N, int NP, bool SP, bool Z>
 int launch_bwd_t(const MMParams& p, cudaStream_t stream) {
-    using Cf = MMCfg<N>;
-    const size_t smem = bwd_smem_bytes<N>();
+    using Cf = MMCfg<N, NP>;
+    const size_t smem = bwd_smem_bytes<N, NP>();
     static int attr_done[MMB_MAX_DEVICES] = {};
-    const int st = mmb_smem_attr(mmscan_bwd_kernel<N, SP, Z>, smem, attr_done);
+    const int st = mmb_smem_attr(mmscan_bwd_kernel<N, NP, SP, Z>, smem, attr_done);
     if (st != MMB_OK) return st;
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
-    mmscan_bwd_kernel<N, SP, Z><<<grid, MM_NT, smem, stream>>>(p);
+    mmscan_bwd_kernel<N, NP, SP, Z><<<grid, MM_NT, smem, stream>>>(p);
     return mmb_launch_status();
 }
 
-template <int N>
-int launch_fwd(const MMParams& p, cudaStream_t stream) {
+template <int N, int NP>
+int launch_fwd_np(const MMParams& p, cudaStream_t s) {
     const bool z = p.z != nullptr;
-    if (p.softplus) return z ? launch_fwd_t<N, true, true>(p, stream) : launch_fwd_t<N, true, false>(p, stream);
-    return z ? launch_fwd_t<N, false, true>(p, stream) : launch_fwd_t<N, false, false>(p, stream);
+    if (p.softplus)
+        return z ? launch_fwd_t<N, NP, true, true>(p, s) : launch_fwd_t<N, NP, true, false>(p, s);
+    return z ? launch_fwd_t<N, NP, false, true>(p, s) : launch_fwd_t<N, NP, false, false>(p, s);
 }
 
-template <int N>
-int launch_bwd(const MMParams& p, cudaStream_t stream) {
+template <int N, int NP>
+int launch_bwd_np(const MMParams& p, cudaStream_t s) {
     const bool z = p.z != nullptr;
-    if (p.softplus) return z ? launch_bwd_t<N, true, true>(p, stream) : launch_bwd_t<N, true, false>(p, stream);
-    return z ? launch_bwd_t<N, false, true>(p, stream) : launch_bwd_t<N, false, false>(p, stream);
+    if (p.softplus)
+        return z ? launch_bwd_t<N, NP, true, true>(p, s) : launch_bwd_t<N, NP, true, false>(p, s);
+    return z ? launch_bwd_t<N, NP, false, true>(p, s) : launch_bwd_t<N, NP, false, false>(p, s);
+}
+
+// States per thread: 2 when 4 would leave the GPU with fewer than ~16 warps per
+// SM (too few to hide the recurrence's latency), else 4.  The forward and the
+// backward of one call must agree (the checkpoint layout depends on it), so
+// this depends only on the shape.
+#ifndef MMB_NP2_THRESHOLD_WARPS_PER_SM
+#define MMB_NP2_THRESHOLD_WARPS_PER_SM 2
+#endif
+static int states_per_thread(const MMParams& p, int64_t N) {
+    if (N == 64) return 4;
+    const int64_t threads4 = p.Bsz * p.D * (N / 4);
+    return threads4 < (int64_t)148 * MMB_NP2_THRESHOLD_WARPS_PER_SM * 32 ? 2 : 4;
 }
 
 static bool aligned16(const void* ptr) { return ptr == nullptr || ((uintptr_t)ptr & 15) == 0; }
@@ -712,11 +707,12 @@ extern "C" int mmb_mmscan_fwd(const mmb_mmscan_desc* desc, const float* x, const
     p.out = out;
     p.ckpt = ckpt;
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    const bool two = states_per_thread(p, desc->dstate) == 2;
     switch (desc->dstate) {
-        case 8: return launch_fwd<8>(p, s);
-        case 16: return launch_fwd<16>(p, s);
-        case 32: return launch_fwd<32>(p, s);
-        default: return launch_fwd<64>(p, s);
+        case 8: return two ? launch_fwd_np<8, 2>(p, s) : launch_fwd_np<8, 4>(p, s);
+        case 16: return two ? launch_fwd_np<16, 2>(p, s) : launch_fwd_np<16, 4>(p, s);
+        case 32: return two ? launch_fwd_np<32, 2>(p, s) : launch_fwd_np<32, 4>(p, s);
+        default: return launch_fwd_np<64, 4>(p, s);
     }
 }
 
@@ -750,10 +746,11 @@ extern "C" int mmb_mmscan_bwd(const mmb_mmscan_desc* desc, const float* x, const
         return MMB_ERR_LAUNCH;
     if (p.ddbias && cudaMemsetAsync(p.ddbias, 0, (size_t)p.D * sizeof(float), s) != cudaSuccess)
         return MMB_ERR_LAUNCH;
+    const bool two = states_per_thread(p, N) == 2;
     switch (N) {
-        case 8: return launch_bwd<8>(p, s);
-        case 16: return launch_bwd<16>(p, s);
-        case 32: return launch_bwd<32>(p, s);
-        default: return launch_bwd<64>(p, s);
+        case 8: return two ? launch_bwd_np<8, 2>(p, s) : launch_bwd_np<8, 4>(p, s);
+        case 16: return two ? launch_bwd_np<16, 2>(p, s) : launch_bwd_np<16, 4>(p, s);
+        case 32: return two ? launch_bwd_np<32, 2>(p, s) : launch_bwd_np<32, 4>(p, s);
+        default: return launch_bwd_np<64, 4>(p, s);
     }
 }

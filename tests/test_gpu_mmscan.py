@@ -104,6 +104,10 @@ CASES = [
     (2, 50, 12, 4, False, False, True, 0.6, 1.0),   # N=4 runs padded to 8
     (2, 70, 16, 12, True, False, True, 0.0, 1.0),   # N=12 runs padded to 16, beta = 0
     (1, 300, 128, 16, True, True, True, 0.95, 2.0),
+    # many channels: 4 states per thread (fewer channels run 2 per thread)
+    (48, 40, 512, 16, True, True, True, 0.9, 1.0),
+    (40, 21, 1000, 8, True, False, True, 0.5, 1.0),
+    (20, 33, 520, 32, False, True, True, 0.7, 1.0),
 ]
 
 
