@@ -68,6 +68,14 @@ const char* mmb_last_error(void);
  * and strides that are multiples of 4 take the vector path; anything else works
  * with 4-byte copies.
  * ========================================================================= */
+
+/* Element type of the activations x, delta, z, B, C, out, dout, dx, ddelta, dz
+ * (desc.dtype).  A, D, delta_bias, dA, dB, dC, dD, ddelta_bias, states and
+ * checkpoints are fp32 in every case; state and arithmetic are always fp32.
+ * bf16 calls need 16-byte aligned activation pointers and dim and every stride
+ * a multiple of 8 (MMB_ERR_ALIGN otherwise). */
+enum mmb_dtype { MMB_F32 = 0, MMB_BF16 = 1 };
+
 typedef struct mmb_mmscan_desc {
     int64_t batch, seqlen, dim, dstate;
     int64_t x_stride[2];     /* (batch, seq) strides of x     */
@@ -77,7 +85,7 @@ typedef struct mmb_mmscan_desc {
     int64_t C_stride[2];     /* (batch, seq) strides of C     */
     float beta, alpha;
     int32_t delta_softplus;
-    int32_t reserved;
+    int32_t dtype;           /* enum mmb_dtype (0 = fp32)     */
 } mmb_mmscan_desc;
 
 /* Floats of checkpoint workspace the forward writes for the backward
@@ -85,7 +93,9 @@ typedef struct mmb_mmscan_desc {
 size_t mmb_mmscan_ckpt_floats(int64_t batch, int64_t seqlen, int64_t dim, int64_t dstate);
 
 /* Forward.  D, z, delta_bias nullable.  ckpt nullable (inference: no
- * checkpoints); the backward needs the checkpoints of the same call. */
+ * checkpoints); the backward needs the checkpoints of the same call.
+ * fp32 activations only (desc->dtype == MMB_F32); mmb_mmscan_forward takes
+ * either type and the segment carries. */
 int mmb_mmscan_fwd(const mmb_mmscan_desc* desc, const float* x, const float* delta,
                    const float* A, const float* B, const float* C, const float* D,
                    const float* z, const float* delta_bias, float* out, float* ckpt,
@@ -100,6 +110,92 @@ int mmb_mmscan_bwd(const mmb_mmscan_desc* desc, const float* x, const float* del
                    const float* dout, float* dx, float* ddelta, float* dA, float* dB,
                    float* dC, float* dD, float* dz, float* ddelta_bias,
                    mmb_stream_t stream);
+
+/* -------------------------------------------------------------------------
+ * The same scan with bf16 or fp32 activations and segment carries, for a
+ * sequence split into consecutive segments (one per GPU when a long sequence
+ * is sharded along time; each segment is one call with seqlen = its length).
+ * The reference has no counterpart: its scan always covers the whole sequence.
+ *
+ * States are (batch, dim, 2, dstate) fp32: [h | v] for the forward state,
+ * [lam | mu] = [a_t gh_t | gv_t] for the adjoint pair at a segment boundary.
+ * Over a segment of T steps,
+ *   forward   h_T = P h_0 + beta Q' v_0 + h^0 ,     v_T = beta^T v_0 + v^0
+ *   adjoint   lam_0 = P lam_T + lam^0 ,             mu_0 = Q' lam_T + beta^T mu_T + mu^0
+ * where P = prod a_t, Q' = sum_t beta^(t-1) prod_{s>t} a_s, (h^0, v^0) is the
+ * end state from a zero start and (lam^0, mu^0) the pair leaving the first
+ * step when none arrives.  The summaries below compute those coefficients so
+ * every segment's incoming carry follows from one all-gather.
+ * ------------------------------------------------------------------------- */
+typedef struct mmb_mmscan_tensors {
+    /* inputs (activations in desc->dtype; the rest fp32) */
+    const void* x;
+    const void* delta;
+    const void* z;            /* nullable */
+    const void* B;
+    const void* C;
+    const float* A;
+    const float* D;           /* nullable */
+    const float* delta_bias;  /* nullable */
+    const float* state_in;    /* nullable: [h | v] before the first step (zeros) */
+    const float* gstate_in;   /* nullable: [lam | mu] arriving from after the last
+                                 step (zeros); needs seqlen % 8 == 0 */
+    const void* dout;         /* backward */
+    /* outputs */
+    void* out;                /* forward, (batch, seqlen, dim) */
+    float* state_out;         /* nullable: [h | v] after the last step */
+    float* ckpt;              /* forward writes (nullable), backward reads */
+    void* dx;                 /* backward, (batch, seqlen, dim) */
+    void* ddelta;
+    void* dz;                 /* nullable */
+    float* dA;                /* backward, fp32 sums */
+    float* dB;
+    float* dC;
+    float* dD;                /* nullable */
+    float* ddelta_bias;       /* nullable */
+    float* gstate_out;        /* nullable: [lam | mu] leaving the first step */
+} mmb_mmscan_tensors;
+
+/* Forward with either activation type and optional state_in / state_out.
+ * Reads x, delta, z, B, C, A, D, delta_bias, state_in; writes out, ckpt,
+ * state_out.  The backward of a segment reads the checkpoints its forward
+ * wrote, which start from state_in. */
+int mmb_mmscan_forward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t,
+                       mmb_stream_t stream);
+
+/* Backward with either activation type and optional gstate_in / gstate_out.
+ * Reads x, delta, z, B, C, A, D, delta_bias, ckpt, dout, gstate_in; writes dx,
+ * ddelta, dz, dA, dB, dC, dD, ddelta_bias (dA, dB, dC, dD, ddelta_bias are
+ * fp32 sums for either type) and gstate_out. */
+int mmb_mmscan_backward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t,
+                        mmb_stream_t stream);
+
+/* Forward segment summary: summary (batch, dim, 4, dstate) = [h^0 | v^0 | P | Q'].
+ * Reads x, delta, B, A, delta_bias. */
+int mmb_mmscan_fwd_summary(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t,
+                           float* summary, mmb_stream_t stream);
+
+/* Backward segment summary: gsummary (batch, dim, 2, dstate) = [lam^0 | mu^0].
+ * Reads delta, z, dout, C, A, delta_bias. */
+int mmb_mmscan_bwd_summary(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t,
+                           float* gsummary, mmb_stream_t stream);
+
+#define MMB_MAX_SEGMENTS 64
+
+/* Incoming forward state of segment `seg` of `nseg` (seg_len: host array of
+ * the segments' lengths; summaries: (nseg, batch, dim, 4, dstate), segment j's
+ * forward summary at j): folds segments 0..seg-1 into state_in (batch, dim, 2,
+ * dstate).  nseg <= MMB_MAX_SEGMENTS. */
+int mmb_mmscan_carry_fwd(int64_t nseg, int64_t seg, const int64_t* seg_len, int64_t batch,
+                         int64_t dim, int64_t dstate, float beta, const float* summaries,
+                         float* state_in, mmb_stream_t stream);
+
+/* Incoming adjoint pair of segment `seg`: folds segments nseg-1 down to seg+1
+ * (their forward summaries for P, Q' and gsummaries (nseg, batch, dim, 2,
+ * dstate) for lam^0, mu^0) into gstate_in (batch, dim, 2, dstate). */
+int mmb_mmscan_carry_bwd(int64_t nseg, int64_t seg, const int64_t* seg_len, int64_t batch,
+                         int64_t dim, int64_t dstate, float beta, const float* summaries,
+                         const float* gsummaries, float* gstate_in, mmb_stream_t stream);
 
 /* =========================================================================
  * Row scan:  v_t = beta*v_{t-1} + u_t ;  h_t = a_t*h_{t-1} + v_t  over the rows

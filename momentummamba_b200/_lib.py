@@ -30,8 +30,24 @@ class MMScanDesc(ctypes.Structure):
         ("batch", _c_i64), ("seqlen", _c_i64), ("dim", _c_i64), ("dstate", _c_i64),
         ("x_stride", _c_i64 * 2), ("delta_stride", _c_i64 * 2), ("z_stride", _c_i64 * 2),
         ("B_stride", _c_i64 * 2), ("C_stride", _c_i64 * 2),
-        ("beta", _c_f), ("alpha", _c_f), ("delta_softplus", _c_i32), ("reserved", _c_i32),
+        ("beta", _c_f), ("alpha", _c_f), ("delta_softplus", _c_i32), ("dtype", _c_i32),
     ]
+
+
+MMB_F32, MMB_BF16 = 0, 1
+
+
+class MMScanTensors(ctypes.Structure):
+    """mirror of struct mmb_mmscan_tensors (device pointers; None = NULL)"""
+    _fields_ = [(name, _c_p) for name in (
+        "x", "delta", "z", "B", "C", "A", "D", "delta_bias", "state_in", "gstate_in", "dout",
+        "out", "state_out", "ckpt", "dx", "ddelta", "dz", "dA", "dB", "dC", "dD",
+        "ddelta_bias", "gstate_out")]
+
+
+_DESC_P = ctypes.POINTER(MMScanDesc)
+_TENS_P = ctypes.POINTER(MMScanTensors)
+_I64_P = ctypes.POINTER(_c_i64)
 
 
 # name -> (restype, argtypes)
@@ -42,6 +58,14 @@ _SIGNATURES = {
     "mmb_mmscan_ckpt_floats": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "mmb_mmscan_fwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 10 + [_c_p]),
     "mmb_mmscan_bwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 18 + [_c_p]),
+    "mmb_mmscan_forward": (ctypes.c_int, [_DESC_P, _TENS_P, _c_p]),
+    "mmb_mmscan_backward": (ctypes.c_int, [_DESC_P, _TENS_P, _c_p]),
+    "mmb_mmscan_fwd_summary": (ctypes.c_int, [_DESC_P, _TENS_P, _c_p, _c_p]),
+    "mmb_mmscan_bwd_summary": (ctypes.c_int, [_DESC_P, _TENS_P, _c_p, _c_p]),
+    "mmb_mmscan_carry_fwd": (ctypes.c_int, [_c_i64, _c_i64, _I64_P, _c_i64, _c_i64, _c_i64, _c_f,
+                                            _c_p, _c_p, _c_p]),
+    "mmb_mmscan_carry_bwd": (ctypes.c_int, [_c_i64, _c_i64, _I64_P, _c_i64, _c_i64, _c_i64, _c_f,
+                                            _c_p, _c_p, _c_p, _c_p]),
     "mmb_rows_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p]),
     "mmb_rows_bwd": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p]),
     "mmb_pscan_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p]),

@@ -24,8 +24,8 @@ NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC", "-Xcompiler", "-O2",
-    "--shared",
 ]
+OBJ_DIR = os.path.join(PKG, "_build")
 
 
 def _nvcc() -> str:
@@ -54,13 +54,27 @@ def is_stale() -> bool:
 
 
 def build(force: bool = False, verbose: bool = False) -> str:
+    """Compile every .cu unit (in parallel) and link the shared library."""
     if not force and not is_stale():
         return LIB_PATH
+    nvcc = _nvcc()
+    os.makedirs(OBJ_DIR, exist_ok=True)
+    inc = ["-I", os.path.join(ROOT, "include")]
+    jobs = []
+    for src in sources():
+        obj = os.path.join(OBJ_DIR, os.path.basename(src)[:-3] + ".o")
+        cmd = [nvcc, *NVCC_FLAGS, *inc, "-c", src, "-o", obj]
+        if verbose:
+            print(" ".join(cmd))
+        jobs.append((obj, subprocess.Popen(cmd)))
+    failed = [obj for obj, proc in jobs if proc.wait() != 0]
+    if failed:
+        raise RuntimeError("nvcc failed for " + ", ".join(os.path.basename(f) for f in failed))
     tmp = LIB_PATH + ".tmp"
-    cmd = [_nvcc(), *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-o", tmp, *sources()]
+    link = [nvcc, *NVCC_FLAGS, "--shared", "-o", tmp, *[obj for obj, _ in jobs]]
     if verbose:
-        print(" ".join(cmd))
-    subprocess.run(cmd, check=True)
+        print(" ".join(link))
+    subprocess.run(link, check=True)
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
 

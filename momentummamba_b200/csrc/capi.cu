@@ -1,7 +1,7 @@
 // Status strings and ABI version of the C interface.
 #include "mmb_common.cuh"
 
-#define MMB_ABI_VERSION 1
+#define MMB_ABI_VERSION 2
 
 extern "C" const char* mmb_status_string(int status) {
     switch (status) {

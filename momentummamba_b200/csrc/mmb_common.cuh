@@ -70,6 +70,64 @@ __device__ __forceinline__ void stage_tile(float* s, const float* g, int64_t gst
     }
 }
 
+// 16-bit elements (bf16 activations): stage a ROWS x COLS tile of 2-byte values
+// with 16-byte copies; the caller guarantees COLS % 8 == 0, 16-byte aligned
+// rows and cvalid % 8 == 0.  Out-of-range rows and columns are zero-filled.
+template <int ROWS, int COLS, int SPITCH, int NTHREADS>
+__device__ __forceinline__ void stage_tile_b16(uint16_t* s, const uint16_t* g, int64_t gstride,
+                                               int rvalid, int cvalid, int tid) {
+    constexpr int C8 = COLS / 8;
+    constexpr int TOTAL = ROWS * C8;
+#pragma unroll
+    for (int i = tid; i < TOTAL; i += NTHREADS) {
+        const int r = i / C8, c = (i % C8) * 8;
+        const bool ok = (r < rvalid) && (c < cvalid);
+        const uint16_t* src = ok ? g + (int64_t)r * gstride + c : g;
+        cp_async16(s + r * SPITCH + c, src, ok);
+    }
+}
+
+// bf16 -> fp32 is exact: the bf16 bits are the high half of the fp32 word.
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Widen a staged ROWS x COLS bf16 tile (pitch SPIN) into an fp32 tile (pitch
+// SPOUT, a multiple of 4).
+template <int ROWS, int COLS, int SPIN, int SPOUT, int NTHREADS>
+__device__ __forceinline__ void widen_tile(float* dst, const uint16_t* src, int tid) {
+    constexpr int C8 = COLS / 8;
+    constexpr int TOTAL = ROWS * C8;
+#pragma unroll
+    for (int i = tid; i < TOTAL; i += NTHREADS) {
+        const int r = i / C8, c = (i % C8) * 8;
+        const uint4 q = *reinterpret_cast<const uint4*>(src + r * SPIN + c);
+        float4* o = reinterpret_cast<float4*>(dst + r * SPOUT + c);
+        o[0] = make_float4(bf16_lo(q.x), bf16_hi(q.x), bf16_lo(q.y), bf16_hi(q.y));
+        o[1] = make_float4(bf16_lo(q.z), bf16_hi(q.z), bf16_lo(q.w), bf16_hi(q.w));
+    }
+}
+
+// fp32 -> bf16, round to nearest even (NaN kept quiet).
+__device__ __forceinline__ uint16_t f32_to_bf16(float f) {
+    const uint32_t u = __float_as_uint(f);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return (uint16_t)((u >> 16) | 0x40u);
+    return (uint16_t)((u + 0x7fffu + ((u >> 16) & 1u)) >> 16);
+}
+
+// Element types of the activations: fp32 or bf16 (stored as raw 16-bit words).
+struct ElemF32 {
+    using T = float;
+    static constexpr int BYTES = 4;
+    __device__ static float load(const T* p, int64_t i) { return p[i]; }
+    __device__ static void store(T* p, int64_t i, float v) { p[i] = v; }
+};
+struct ElemBF16 {
+    using T = uint16_t;
+    static constexpr int BYTES = 2;
+    __device__ static float load(const T* p, int64_t i) { return bf16_lo(p[i]); }
+    __device__ static void store(T* p, int64_t i, float v) { p[i] = f32_to_bf16(v); }
+};
+
 // ---------------------------------------------------------------------------
 // math
 // ---------------------------------------------------------------------------

@@ -1,0 +1,7 @@
+// Momentum scan backward and backward-summary kernels for bf16 activations (one
+// compilation unit per element type and side, so they build in parallel).
+#include "mmscan_kernels.cuh"
+
+namespace mmb {
+template int mmscan_launch<ElemBF16, false>(const MMParams&, int64_t, int, int, cudaStream_t);
+}  // namespace mmb

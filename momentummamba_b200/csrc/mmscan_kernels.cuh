@@ -1,0 +1,1021 @@
+// Fused momentum selective scan for sm_100a: forward, backward, and the
+// segment summaries used when one sequence is split into consecutive segments
+// (one per GPU).
+//
+// Work decomposition: one CTA of 128 threads owns one sequence b and a tile of
+// DT = 128 / G channels for the whole sequence, G = N / NP lanes per channel; a
+// thread owns one channel d and NP (2 or 4) of its N states, h and v in
+// registers, updated with packed fp32 pairs (sm_100 f32x2 FMA).  NP is picked
+// per call: 2 when the problem is so small that 4 states per thread would leave
+// the SMs under two warps each, else 4 (fewer cross-lane sums; measured faster
+// from B*D = 8192 channels up).  The sequence is streamed through shared memory
+// in chunks of T = 32 steps with double-buffered cp.async (x, delta, z, B, C
+// tiles; rows of the (B, L, D) tensors are coalesced 16-byte copies).  bf16
+// activations are staged as raw 16-bit tiles and widened to fp32 in shared
+// memory once per chunk; state, arithmetic and accumulation stay fp32.
+//
+// Per 8-step block, each lane owns 8/G (t, d) items of its channel (at least
+// one): it computes softplus(delta + bias), alpha*dt*x and the SiLU(z) gate for
+// them once, the per-step scalars are shuffled to the channel's lanes, the
+// block's decay factors exp(dt*A) are issued before the recurrence, and the
+// channel's partial sums of y = C h are reduce-scattered so each lane finishes
+// its own items.
+//
+// The forward stores (h, v) every 8 steps as checkpoints.  The backward walks
+// the sequence in reverse, 8 steps at a time: it recomputes the window forward
+// from its checkpoint into registers (a_t and h_t), then runs the adjoint
+// backwards through it:
+//   gh_t = dy_t C_t + a_{t+1} gh_{t+1} ;  gv_t = gh_t + beta gv_{t+1}
+// The n-sums (dx, ddelta, recomputed y) are reduce-scattered back to the
+// owning lanes; the d-sums of the dB | dC contributions go through a per-warp
+// shared window buffer and vector reductions to global memory; dA, dD and
+// d(delta_bias) accumulate in registers over the sequence.
+//
+// Segments.  Over a segment of T steps the forward state maps affinely,
+//   h_T = P h_0 + beta Q' v_0 + h^0 ,   v_T = beta^T v_0 + v^0 ,
+// with (h^0, v^0) the segment's end state from zero, P = prod a_t and
+// Q' = sum_t beta^(t-1) prod_{s>t} a_s; the adjoint pair (lam, mu) = (a gh, gv)
+// crossing the segment from its end to its start maps with the same P and Q':
+//   lam_0 = P lam_T + lam^0 ,   mu_0 = Q' lam_T + beta^T mu_T + mu^0 .
+// The summary kernels compute (h^0, v^0, P, Q') and (lam^0, mu^0); the forward
+// takes the incoming state (state_in) and the backward the incoming adjoint
+// pair (gstate_in).
+#pragma once
+
+#include "mmb_common.cuh"
+
+namespace mmb {
+
+constexpr int MM_NT = 128;  // threads per CTA
+constexpr int MM_T = 32;    // steps per staged chunk
+constexpr int MM_CK = 8;    // checkpoint interval = steps per register block
+constexpr unsigned FULL = 0xffffffffu;
+// cp.async pipeline depth in chunks (3 and 4 stages measured no faster: the
+// kernels are issue-latency bound, not load-latency bound)
+constexpr int MM_NS = 2;
+
+__host__ __device__ constexpr int ilog2c(int v) { return v <= 1 ? 0 : 1 + ilog2c(v / 2); }
+
+template <int N, int NP>
+struct MMCfg {
+    static constexpr int NP2 = NP / 2;                // packed pairs per thread
+    static constexpr int G = N / NP;                  // lanes per channel
+    static constexpr int LOG2G = ilog2c(G);
+    static constexpr int LB = LOG2G < 3 ? LOG2G : 3;  // lane bits that split an 8-step block
+    static constexpr int IPL = MM_CK >> LB;           // (t, d) items a lane owns per block
+    static constexpr int DT = MM_NT / G;              // channels per CTA
+    static constexpr int DPW = 32 / G;                // channels per warp
+    static constexpr int LOG2DPW = 5 - LOG2G;
+    // (T x DT) fp32 tile pitch: the rows and channels a warp reads at once fall
+    // in distinct banks
+    static constexpr int RP = G >= 16 ? DT + 4 : DT + DPW;
+    static constexpr int TR = MM_T * RP;
+    static constexpr int TN = MM_T * N;
+    static_assert((NP == 2 || NP == 4) && N % NP == 0 && G >= 2 && G <= 16, "unsupported shape");
+};
+
+// Shared-memory layout of one kernel: NDT (T x DT) activation tiles and two
+// (T x N) tiles per chunk.  fp32 activations: MM_NS fp32 stages.  bf16: one
+// fp32 working stage plus MM_NS raw 16-bit stages that cp.async fills.
+template <int N, int NP, int NDT, int EBYTES>
+struct MMSmem {
+    using Cf = MMCfg<N, NP>;
+    static constexpr bool WIDE = EBYTES == 2;
+    static constexpr int F32 = NDT * Cf::TR + 2 * Cf::TN;             // floats per fp32 stage
+    static constexpr int RAW = NDT * MM_T * Cf::DT + 2 * MM_T * N;    // 16-bit words per raw stage
+    static constexpr int FLOATS = WIDE ? F32 + MM_NS * RAW / 2 : MM_NS * F32;
+};
+
+// Lane (within its channel's group) that owns step s of an 8-step block: the
+// inverse of the reduce-scatter placement rs_index<8, LB>.
+template <int LB>
+__host__ __device__ constexpr int block_owner(int s) {
+    int ng = 0;
+    for (int b = 0; b < LB; ++b)
+        if ((s >> (2 - b)) & 1) ng |= 1 << b;
+    return ng;
+}
+
+// NP consecutive floats of shared memory as packed pairs.
+template <int NP>
+__device__ __forceinline__ void ld_pairs(const float* p, float2 (&o)[NP / 2]) {
+    if constexpr (NP == 4) {
+        const float4 q = *reinterpret_cast<const float4*>(p);
+        o[0] = make_float2(q.x, q.y);
+        o[1] = make_float2(q.z, q.w);
+    } else {
+        o[0] = *reinterpret_cast<const float2*>(p);
+    }
+}
+
+// NP consecutive floats of global memory as packed pairs, and back.
+template <int NP>
+__device__ __forceinline__ void ld_pairs_g(const float* p, float2 (&o)[NP / 2]) {
+#pragma unroll
+    for (int j = 0; j < NP / 2; ++j) o[j] = reinterpret_cast<const float2*>(p)[j];
+}
+template <int NP>
+__device__ __forceinline__ void st_pairs_g(float* p, const float2 (&o)[NP / 2]) {
+#pragma unroll
+    for (int j = 0; j < NP / 2; ++j) reinterpret_cast<float2*>(p)[j] = o[j];
+}
+
+// sum_j c_j h_j over this thread's NP states
+template <int NP2>
+__device__ __forceinline__ float dot_pairs(const float2 (&c)[NP2], const float2 (&h)[NP2]) {
+    float2 acc = fmul2(c[0], h[0]);
+#pragma unroll
+    for (int j = 1; j < NP2; ++j) acc = ffma2(c[j], h[j], acc);
+    return acc.x + acc.y;
+}
+
+struct MMParams {
+    int64_t Bsz, L, D;
+    // activations: element type of the call (fp32 or bf16)
+    const void *x, *delta, *z, *Bm, *Cm;
+    const float *A, *Dskip, *dbias;
+    int64_t xs[2], ds[2], zs[2], bs[2], cs[2];
+    float beta, alpha;
+    int softplus;
+    int vec;  // 16-byte staging allowed
+    const float* state_in;  // (Bsz, D, 2, N): h | v before the first step, or null
+    float* state_out;       // (Bsz, D, 2, N) after the last step, or null
+    const float* ckpt_in;
+    float* ckpt;
+    void* out;
+    float* summary;  // forward summary (Bsz, D, 4, N) or backward summary (Bsz, D, 2, N)
+    // backward
+    const void* dout;
+    const float* gstate_in;  // (Bsz, D, 2, N): a gh | gv arriving from after the last step
+    float* gstate_out;       // (Bsz, D, 2, N): a gh | gv leaving the first step
+    void *dx, *ddelta, *dz;
+    float *dA, *dB, *dC, *dD, *ddbias;
+};
+
+// checkpoint record of (b, window k, channel d): 2N floats, lane ng's
+// [h(NP) | v(NP)] at ng * 2 * NP
+__device__ __forceinline__ int64_t ckpt_base(const MMParams& p, int64_t b, int64_t k, int64_t d,
+                                             int N) {
+    const int64_t K = (p.L + MM_CK - 1) / MM_CK;
+    return ((b * K + k) * p.D + d) * (int64_t)(2 * N);
+}
+
+template <int NP>
+__device__ __forceinline__ void ckpt_store(float* dst, const float2 (&h)[NP / 2],
+                                           const float2 (&v)[NP / 2]) {
+    if constexpr (NP == 4) {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(h[0].x, h[0].y, h[1].x, h[1].y);
+        reinterpret_cast<float4*>(dst)[1] = make_float4(v[0].x, v[0].y, v[1].x, v[1].y);
+    } else {
+        reinterpret_cast<float4*>(dst)[0] = make_float4(h[0].x, h[0].y, v[0].x, v[0].y);
+    }
+}
+
+template <int NP>
+__device__ __forceinline__ void ckpt_load(const float* src, float2 (&h)[NP / 2],
+                                          float2 (&v)[NP / 2]) {
+    if constexpr (NP == 4) {
+        const float4 a = reinterpret_cast<const float4*>(src)[0];
+        const float4 c = reinterpret_cast<const float4*>(src)[1];
+        h[0] = make_float2(a.x, a.y); h[1] = make_float2(a.z, a.w);
+        v[0] = make_float2(c.x, c.y); v[1] = make_float2(c.z, c.w);
+    } else {
+        const float4 a = reinterpret_cast<const float4*>(src)[0];
+        h[0] = make_float2(a.x, a.y);
+        v[0] = make_float2(a.z, a.w);
+    }
+}
+
+// Chunk staging shared by the kernels: D-tile i of a chunk holds (T x DT)
+// activations, N-tile j (T x N) of B or C.  `slot` is the pipeline stage.
+template <int N, int NP, int NDT, class E>
+struct MMStager {
+    using Cf = MMCfg<N, NP>;
+    using Sm = MMSmem<N, NP, NDT, E::BYTES>;
+    using ET = typename E::T;
+    float* smem;
+    int tid, dcols, vec;
+
+    __device__ uint16_t* raw(int slot) const {
+        return reinterpret_cast<uint16_t*>(smem + Sm::F32) + slot * Sm::RAW;
+    }
+    __device__ void tile_d(int slot, int i, const ET* g, int64_t gstride, int rows) const {
+        if constexpr (Sm::WIDE)
+            stage_tile_b16<MM_T, Cf::DT, Cf::DT, MM_NT>(raw(slot) + i * MM_T * Cf::DT,
+                                                        reinterpret_cast<const uint16_t*>(g),
+                                                        gstride, rows, dcols, tid);
+        else
+            stage_tile<MM_T, Cf::DT, Cf::RP, MM_NT>(smem + slot * Sm::F32 + i * Cf::TR,
+                                                    reinterpret_cast<const float*>(g), gstride,
+                                                    rows, dcols, vec, tid);
+    }
+    __device__ void tile_n(int slot, int j, const ET* g, int64_t gstride, int rows) const {
+        if constexpr (Sm::WIDE)
+            stage_tile_b16<MM_T, N, N, MM_NT>(raw(slot) + NDT * MM_T * Cf::DT + j * MM_T * N,
+                                              reinterpret_cast<const uint16_t*>(g), gstride, rows,
+                                              N, tid);
+        else
+            stage_tile<MM_T, N, N, MM_NT>(smem + slot * Sm::F32 + NDT * Cf::TR + j * Cf::TN,
+                                          reinterpret_cast<const float*>(g), gstride, rows, N,
+                                          vec, tid);
+    }
+    // After the stage's copies landed (and a barrier): the fp32 view of it.
+    // bf16 widens the tiles named by the masks into the working stage; the
+    // caller places a barrier between this and the first read.
+    __device__ const float* view(int slot, unsigned dmask, unsigned nmask) const {
+        if constexpr (Sm::WIDE) {
+            const uint16_t* r = raw(slot);
+#pragma unroll
+            for (int i = 0; i < NDT; ++i)
+                if (dmask & (1u << i))
+                    widen_tile<MM_T, Cf::DT, Cf::DT, Cf::RP, MM_NT>(smem + i * Cf::TR,
+                                                                    r + i * MM_T * Cf::DT, tid);
+#pragma unroll
+            for (int j = 0; j < 2; ++j)
+                if (nmask & (1u << j))
+                    widen_tile<MM_T, N, N, N, MM_NT>(smem + NDT * Cf::TR + j * Cf::TN,
+                                                     r + NDT * MM_T * Cf::DT + j * MM_T * N, tid);
+            return smem;
+        } else {
+            return smem + slot * Sm::F32;
+        }
+    }
+};
+
+// ---------------------------------------------------------------------------
+// forward (SUMM: the segment summary instead -- no C, z, y or checkpoints)
+// ---------------------------------------------------------------------------
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, bool SUMM>
+__global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
+    using Cf = MMCfg<N, NP>;
+    using ET = typename E::T;
+    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, RP = Cf::RP, IPL = Cf::IPL, LB = Cf::LB;
+    constexpr int NP2 = Cf::NP2, NBLK = T / MM_CK;
+    static_assert(!(SUMM && HAS_Z), "the summary has no gate");
+    extern __shared__ float4 smem4[];
+    // tiles: x | delta | z (T x RP), B | C (T x N)
+    MMStager<N, NP, 3, E> stg{reinterpret_cast<float*>(smem4), (int)threadIdx.x, 0, p.vec};
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ng = lane & (G - 1);
+    const int lane_base = lane & ~(G - 1);
+    const int ibase = rs_index<MM_CK, LB>(ng & ((1 << LB) - 1), 0);
+    const bool item_lane = (ng >> LB) == 0;  // G = 16: the upper 8 lanes duplicate
+    const int dl = warp * Cf::DPW + (lane >> Cf::LOG2G);
+    const int64_t b = blockIdx.y;
+    const int64_t d0 = (int64_t)blockIdx.x * DT;
+    const int64_t d = d0 + dl;
+    const bool dvalid = d < p.D;
+    stg.dcols = (int)min64(DT, p.D - d0);
+    const ET* gx = static_cast<const ET*>(p.x);
+    const ET* gdl = static_cast<const ET*>(p.delta);
+    const ET* gz = static_cast<const ET*>(p.z);
+    const ET* gB = static_cast<const ET*>(p.Bm);
+    const ET* gC = static_cast<const ET*>(p.Cm);
+    ET* gout = static_cast<ET*>(p.out);
+
+    float2 A2[NP2], h[NP2], v[NP2], Pp[NP2], Qp[NP2];
+#pragma unroll
+    for (int j = 0; j < NP2; ++j) {
+        A2[j] = h[j] = v[j] = Qp[j] = f2(0.f);
+        Pp[j] = f2(1.f);
+        if (dvalid) {
+            const float* Ar = p.A + d * N + ng * NP + 2 * j;
+            A2[j] = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
+        }
+    }
+    if (!SUMM && p.state_in && dvalid) {
+        const float* s = p.state_in + (b * p.D + d) * (2 * N) + ng * NP;
+        ld_pairs_g<NP>(s, h);
+        ld_pairs_g<NP>(s + N, v);
+    }
+    float bpow = 1.f;  // SUMM: beta^(steps so far)
+    const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
+    const float Dv = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
+    const float alpha = p.alpha;
+    const float2 beta2 = f2(p.beta);
+    const int nchunks = (int)((p.L + T - 1) / T);
+    // state before a last, partial 8-step block (exact end state: replayed below)
+    const bool want_end = SUMM || p.state_out != nullptr;
+    int64_t tail_t = -1;
+    float2 hs[NP2], vs[NP2], Ps[NP2], Qs[NP2];
+    float bps = 1.f;
+
+    auto stage = [&](int slot, int c) {
+        const int64_t t0 = (int64_t)c * T;
+        const int rv = (int)min64(T, p.L - t0);
+        stg.tile_d(slot, 0, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
+        stg.tile_d(slot, 1, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1], rv);
+        if (HAS_Z) stg.tile_d(slot, 2, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1], rv);
+        stg.tile_n(slot, 0, gB + b * p.bs[0] + t0 * p.bs[1], p.bs[1], rv);
+        if (!SUMM) stg.tile_n(slot, 1, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
+    };
+    // this lane's items of block k: x, dt, alpha*dt*x
+    auto prep = [&](const float* sx, const float* sdl, int k, float (&xi)[IPL], float (&dti)[IPL],
+                    float (&dtxi)[IPL]) {
+#pragma unroll
+        for (int i = 0; i < IPL; ++i) {
+            const int row = (k * MM_CK + ibase + i) * RP + dl;
+            xi[i] = sx[row];
+            const float r = sdl[row] + bias_d;
+            dti[i] = SOFTPLUS ? softplus_f(r) : r;
+            dtxi[i] = alpha * dti[i] * xi[i];
+        }
+    };
+    constexpr unsigned DMASK = HAS_Z ? 7u : 3u;
+    constexpr unsigned NMASK = SUMM ? 1u : 3u;
+
+#pragma unroll
+    for (int c = 0; c < MM_NS - 1; ++c) {
+        if (c < nchunks) stage(c, c);
+        cp_async_commit();
+    }
+    const float* st = nullptr;
+    for (int c = 0; c < nchunks; ++c) {
+        if (c + MM_NS - 1 < nchunks) stage((c + MM_NS - 1) % MM_NS, c + MM_NS - 1);
+        cp_async_commit();
+        cp_async_wait<MM_NS - 1>();
+        __syncthreads();
+        st = stg.view(c % MM_NS, DMASK, NMASK);
+        if (MMSmem<N, NP, 3, E::BYTES>::WIDE) __syncthreads();
+        const float* sx = st;
+        const float* sdl = st + Cf::TR;
+        const float* sz = st + 2 * Cf::TR;
+        const float* sB = st + 3 * Cf::TR;
+        const float* sC = sB + Cf::TN;
+        const int64_t t0 = (int64_t)c * T;
+
+        float xi[IPL], dti[IPL], dtxi[IPL];
+        prep(sx, sdl, 0, xi, dti, dtxi);
+#pragma unroll
+        for (int k = 0; k < NBLK; ++k) {
+            const int64_t tb = t0 + k * MM_CK;
+            if (tb >= p.L) break;
+            if (want_end && tb + MM_CK > p.L) {
+                tail_t = tb;
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    hs[j] = h[j]; vs[j] = v[j]; Ps[j] = Pp[j]; Qs[j] = Qp[j];
+                }
+                bps = bpow;
+            }
+            // broadcast the block's per-step scalars, then all its decay factors
+            float dts[MM_CK], dtxs[MM_CK];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+                const int src = lane_base | block_owner<LB>(s - s % IPL);
+                dts[s] = __shfl_sync(FULL, dti[s % IPL], src);
+                dtxs[s] = __shfl_sync(FULL, dtxi[s % IPL], src);
+            }
+            float2 a[MM_CK][NP2];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    const float2 e = fmul2(f2(dts[s]), A2[j]);
+                    a[s][j] = make_float2(ex2(e.x), ex2(e.y));
+                }
+            }
+            // next block's items while the exponentials are in flight
+            float nxi[IPL], ndti[IPL], ndtxi[IPL];
+            if (k + 1 < NBLK) prep(sx, sdl, k + 1, nxi, ndti, ndtxi);
+            // checkpoint: state before the block's first step
+            if (!SUMM && p.ckpt && dvalid) {
+                const int64_t kk = tb / MM_CK;
+                ckpt_store<NP>(p.ckpt + ckpt_base(p, b, kk, d, N) + ng * 2 * NP, h, v);
+            }
+            float y[MM_CK];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+                const int tt = k * MM_CK + s;
+                float2 bq[NP2], cq[NP2];
+                ld_pairs<NP>(sB + tt * N + ng * NP, bq);
+                if (!SUMM) ld_pairs<NP>(sC + tt * N + ng * NP, cq);
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    v[j] = ffma2(beta2, v[j], fmul2(f2(dtxs[s]), bq[j]));
+                    h[j] = ffma2(a[s][j], h[j], v[j]);
+                    if (SUMM) {
+                        Pp[j] = fmul2(a[s][j], Pp[j]);
+                        Qp[j] = ffma2(a[s][j], Qp[j], f2(bpow));
+                    }
+                }
+                if (SUMM)
+                    bpow *= p.beta;
+                else
+                    y[s] = dot_pairs(cq, h);
+            }
+            if (!SUMM) {
+                reduce_scatter<MM_CK, 0, Cf::LOG2G>(y, lane);
+                // finish this lane's items: D skip, gate, store
+#pragma unroll
+                for (int i = 0; i < IPL; ++i) {
+                    const int tt = k * MM_CK + ibase + i;
+                    const int64_t gt = t0 + tt;
+                    float o = fmaf(Dv, xi[i], y[i]);
+                    if (HAS_Z) {
+                        const float zv = sz[tt * RP + dl];
+                        o *= zv * sigmoid_f(zv);
+                    }
+                    if (item_lane && dvalid && gt < p.L) E::store(gout, (b * p.L + gt) * p.D + d, o);
+                }
+            }
+            if (k + 1 < NBLK) {
+#pragma unroll
+                for (int i = 0; i < IPL; ++i) {
+                    xi[i] = nxi[i];
+                    dti[i] = ndti[i];
+                    dtxi[i] = ndtxi[i];
+                }
+            }
+        }
+        if (c + 1 < nchunks) __syncthreads();
+    }
+
+    if (!want_end || !dvalid) return;
+    if (tail_t >= 0) {
+        // the last block ran past the end of the sequence: replay its valid
+        // steps from the state saved before it (the last chunk is still staged)
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) {
+            h[j] = hs[j]; v[j] = vs[j]; Pp[j] = Ps[j]; Qp[j] = Qs[j];
+        }
+        bpow = bps;
+        const int64_t t0 = (int64_t)(nchunks - 1) * T;
+        for (int64_t t = tail_t; t < p.L; ++t) {
+            const int tt = (int)(t - t0);
+            const float r = st[Cf::TR + tt * RP + dl] + bias_d;
+            const float dt = SOFTPLUS ? softplus_f(r) : r;
+            const float dtx = alpha * dt * st[tt * RP + dl];
+            float2 bq[NP2];
+            ld_pairs<NP>(st + 3 * Cf::TR + tt * N + ng * NP, bq);
+#pragma unroll
+            for (int j = 0; j < NP2; ++j) {
+                const float2 e = fmul2(f2(dt), A2[j]);
+                const float2 a = make_float2(ex2(e.x), ex2(e.y));
+                v[j] = ffma2(beta2, v[j], fmul2(f2(dtx), bq[j]));
+                h[j] = ffma2(a, h[j], v[j]);
+                if (SUMM) {
+                    Pp[j] = fmul2(a, Pp[j]);
+                    Qp[j] = ffma2(a, Qp[j], f2(bpow));
+                }
+            }
+            if (SUMM) bpow *= p.beta;
+        }
+    }
+    if (SUMM) {
+        float* o = p.summary + (b * p.D + d) * (4 * N) + ng * NP;
+        st_pairs_g<NP>(o, h);
+        st_pairs_g<NP>(o + N, v);
+        st_pairs_g<NP>(o + 2 * N, Pp);
+        st_pairs_g<NP>(o + 3 * N, Qp);
+    } else {
+        float* o = p.state_out + (b * p.D + d) * (2 * N) + ng * NP;
+        st_pairs_g<NP>(o, h);
+        st_pairs_g<NP>(o + N, v);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// backward
+//
+// Chunks of 32 steps in reverse; inside a chunk, 8-step windows in reverse.
+// The d-sums of the dB | dC contributions go through a window buffer
+// [8 steps][DT channels][2N]: each thread stores its NP dB and NP dC terms as
+// units of NP floats (odd channels swap the dB and dC halves, so a warp's
+// stores hit distinct banks); after the window each warp sums its own DPW
+// channels' rows and adds the results to global memory with vector reductions.
+// ---------------------------------------------------------------------------
+// (min 1 block per SM: without it ptxas caps the registers for 3 blocks per SM
+// and spills; the 254-register build measured 7-8 % faster)
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E>
+__global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) {
+    using Cf = MMCfg<N, NP>;
+    using Sm = MMSmem<N, NP, 4, E::BYTES>;
+    using ET = typename E::T;
+    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, RP = Cf::RP, IPL = Cf::IPL, LB = Cf::LB;
+    constexpr int NP2 = Cf::NP2, TR = Cf::TR, DPW = Cf::DPW;
+    constexpr int NQ = 2 * N / 4;  // float4 columns per window-buffer row
+    constexpr int SWZ = NQ / 2;    // float4 swizzle of odd channels (= G units of NP floats)
+    extern __shared__ float4 smem4[];
+    // tiles: x | delta | z | dout (T x RP), B | C (T x N); then the window buffer
+    MMStager<N, NP, 4, E> stg{reinterpret_cast<float*>(smem4), (int)threadIdx.x, 0, p.vec};
+    float* wbuf = reinterpret_cast<float*>(smem4) + Sm::FLOATS;
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ng = lane & (G - 1);
+    const int lane_base = lane & ~(G - 1);
+    const int ibase = rs_index<MM_CK, LB>(ng & ((1 << LB) - 1), 0);
+    const bool item_lane = (ng >> LB) == 0;
+    const int dl = warp * DPW + (lane >> Cf::LOG2G);
+    const int64_t b = blockIdx.y;
+    const int64_t d0 = (int64_t)blockIdx.x * DT;
+    const int64_t d = d0 + dl;
+    const bool dvalid = d < p.D;
+    stg.dcols = (int)min64(DT, p.D - d0);
+    const int swz_units = (dl & 1) ? G : 0;
+    const ET* gx = static_cast<const ET*>(p.x);
+    const ET* gdl = static_cast<const ET*>(p.delta);
+    const ET* gz = static_cast<const ET*>(p.z);
+    const ET* gdo = static_cast<const ET*>(p.dout);
+    const ET* gB = static_cast<const ET*>(p.Bm);
+    const ET* gC = static_cast<const ET*>(p.Cm);
+    ET* gdx = static_cast<ET*>(p.dx);
+    ET* gddl = static_cast<ET*>(p.ddelta);
+    ET* gdz = static_cast<ET*>(p.dz);
+
+    float2 A2[NP2], gh[NP2], gv[NP2], an[NP2], dA[NP2];
+#pragma unroll
+    for (int j = 0; j < NP2; ++j) {
+        A2[j] = gh[j] = gv[j] = an[j] = dA[j] = f2(0.f);
+        if (dvalid) {
+            const float* Ar = p.A + d * N + ng * NP + 2 * j;
+            A2[j] = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
+        }
+    }
+    if (p.gstate_in && dvalid) {
+        // the pair arriving from the step after the sequence enters as
+        // gh = a_L gh_L with a unit factor
+        const float* s = p.gstate_in + (b * p.D + d) * (2 * N) + ng * NP;
+        ld_pairs_g<NP>(s, gh);
+        ld_pairs_g<NP>(s + N, gv);
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) an[j] = f2(1.f);
+    }
+    const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
+    const float Dv = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
+    const float alpha = p.alpha;
+    const float2 beta2 = f2(p.beta);
+    float accD = 0.f, accBias = 0.f;
+    const int nchunks = (int)((p.L + T - 1) / T);
+    float2 nck_h[NP2], nck_v[NP2];  // checkpoint of the next window to process
+#pragma unroll
+    for (int j = 0; j < NP2; ++j) nck_h[j] = nck_v[j] = f2(0.f);
+    auto ck_load = [&](int64_t k) {
+        if (dvalid) ckpt_load<NP>(p.ckpt_in + ckpt_base(p, b, k, d, N) + ng * 2 * NP, nck_h, nck_v);
+    };
+
+    auto stage = [&](int slot, int c) {
+        const int64_t t0 = (int64_t)c * T;
+        const int rv = (int)min64(T, p.L - t0);
+        stg.tile_d(slot, 0, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
+        stg.tile_d(slot, 1, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1], rv);
+        if (HAS_Z) stg.tile_d(slot, 2, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1], rv);
+        stg.tile_d(slot, 3, gdo + (b * p.L + t0) * p.D + d0, p.D, rv);
+        stg.tile_n(slot, 0, gB + b * p.bs[0] + t0 * p.bs[1], p.bs[1], rv);
+        stg.tile_n(slot, 1, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
+    };
+    constexpr unsigned DMASK = HAS_Z ? 15u : 11u;
+
+#pragma unroll
+    for (int it = 0; it < MM_NS - 1; ++it) {
+        if (it < nchunks) stage(it, nchunks - 1 - it);
+        cp_async_commit();
+    }
+    for (int it = 0; it < nchunks; ++it) {
+        const int c = nchunks - 1 - it;
+        if (it + MM_NS - 1 < nchunks) stage((it + MM_NS - 1) % MM_NS, c - (MM_NS - 1));
+        cp_async_commit();
+        cp_async_wait<MM_NS - 1>();
+        __syncthreads();
+        const float* st = stg.view(it % MM_NS, DMASK, 3u);
+        if (Sm::WIDE) __syncthreads();
+        const float* sx = st;
+        const float* sdl = st + TR;
+        const float* sz = st + 2 * TR;
+        const float* sdo = st + 3 * TR;
+        const float* sB = st + 4 * TR;
+        const float* sC = sB + Cf::TN;
+        const int64_t t0 = (int64_t)c * T;
+        const int Lc = (int)min64(T, p.L - t0);
+
+        for (int w = (Lc - 1) / MM_CK; w >= 0; --w) {
+            const int w0 = w * MM_CK;
+            // window checkpoint (loaded one window ahead)
+            if (it == 0 && w == (Lc - 1) / MM_CK) ck_load((t0 + w0) / MM_CK);
+            float2 h[NP2], v[NP2];
+#pragma unroll
+            for (int j = 0; j < NP2; ++j) {
+                h[j] = nck_h[j];
+                v[j] = nck_v[j];
+            }
+            if (t0 + w0 > 0) ck_load((t0 + w0) / MM_CK - 1);
+            // this lane's items: dt, alpha*dt*x, dy = dout*silu(z)
+            float xi[IPL], ri[IPL], dti[IPL], dtxi[IPL], dyi[IPL];
+#pragma unroll
+            for (int i = 0; i < IPL; ++i) {
+                const int row = (w0 + ibase + i) * RP + dl;
+                xi[i] = sx[row];
+                ri[i] = sdl[row] + bias_d;
+                dti[i] = SOFTPLUS ? softplus_f(ri[i]) : ri[i];
+                dtxi[i] = alpha * dti[i] * xi[i];
+                float dy = sdo[row];
+                if (HAS_Z) {
+                    const float zv = sz[row];
+                    dy *= zv * sigmoid_f(zv);
+                }
+                dyi[i] = dy;
+            }
+            float dts[MM_CK], dtxs[MM_CK];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+                const int src = lane_base | block_owner<LB>(s - s % IPL);
+                dts[s] = __shfl_sync(FULL, dti[s % IPL], src);
+                dtxs[s] = __shfl_sync(FULL, dtxi[s % IPL], src);
+            }
+            float2 aa[MM_CK][NP2];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    const float2 e = fmul2(f2(dts[s]), A2[j]);
+                    aa[s][j] = make_float2(ex2(e.x), ex2(e.y));
+                }
+            }
+            // forward replay of the window
+            float2 hh[MM_CK + 1][NP2];
+            float yv[MM_CK];
+#pragma unroll
+            for (int j = 0; j < NP2; ++j) hh[0][j] = h[j];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+                const int tt = w0 + s;
+                float2 bq[NP2], cq[NP2];
+                ld_pairs<NP>(sB + tt * N + ng * NP, bq);
+                ld_pairs<NP>(sC + tt * N + ng * NP, cq);
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    v[j] = ffma2(beta2, v[j], fmul2(f2(dtxs[s]), bq[j]));
+                    h[j] = ffma2(aa[s][j], h[j], v[j]);
+                    hh[s + 1][j] = h[j];
+                }
+                yv[s] = dot_pairs(cq, h);
+            }
+            reduce_scatter<MM_CK, 0, Cf::LOG2G>(yv, lane);
+            float dys[MM_CK];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+                const int src = lane_base | block_owner<LB>(s - s % IPL);
+                dys[s] = __shfl_sync(FULL, dyi[s % IPL], src);
+            }
+            // adjoint sweep
+            float sab[2 * MM_CK];
+            float* wrow = wbuf + dl * 2 * N;
+#pragma unroll
+            for (int s = MM_CK - 1; s >= 0; --s) {
+                const int tt = w0 + s;
+                float2 bq[NP2], cq[NP2];
+                ld_pairs<NP>(sB + tt * N + ng * NP, bq);
+                ld_pairs<NP>(sC + tt * N + ng * NP, cq);
+                const float2 dy2 = f2(dys[s]);
+                float2 sb = f2(0.f), sa = f2(0.f), pb[NP2], pc[NP2];
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    gh[j] = ffma2(an[j], gh[j], fmul2(dy2, cq[j]));
+                    gv[j] = ffma2(beta2, gv[j], gh[j]);
+                    sb = ffma2(gv[j], bq[j], sb);
+                    const float2 t2 = fmul2(fmul2(gh[j], hh[s][j]), aa[s][j]);
+                    sa = ffma2(t2, A2[j], sa);
+                    dA[j] = ffma2(t2, f2(dts[s]), dA[j]);
+                    pb[j] = fmul2(gv[j], f2(dtxs[s]));
+                    pc[j] = fmul2(dy2, hh[s + 1][j]);
+                    an[j] = aa[s][j];
+                }
+                sab[2 * s] = sa.x + sa.y;
+                sab[2 * s + 1] = sb.x + sb.y;
+                // dB | dC terms of (t, d, this lane's states) into the window buffer
+                float* rowp = wrow + s * DT * 2 * N;
+                if constexpr (NP == 4) {
+                    float4* r4 = reinterpret_cast<float4*>(rowp);
+                    r4[ng ^ swz_units] = make_float4(pb[0].x, pb[0].y, pb[1].x, pb[1].y);
+                    r4[(G + ng) ^ swz_units] = make_float4(pc[0].x, pc[0].y, pc[1].x, pc[1].y);
+                } else {
+                    float2* r2 = reinterpret_cast<float2*>(rowp);
+                    r2[ng ^ swz_units] = pb[0];
+                    r2[(G + ng) ^ swz_units] = pc[0];
+                }
+            }
+            // n-sums back to the owning lanes: sab[2i], sab[2i + 1] = (SA, SB) of item i
+            reduce_scatter<2 * MM_CK, 0, Cf::LOG2G>(sab, lane);
+            if (G == 16) sab[1] = __shfl_xor_sync(FULL, sab[0], 8);
+#pragma unroll
+            for (int i = 0; i < IPL; ++i) {
+                const int tt = w0 + ibase + i;
+                const int64_t gt = t0 + tt;
+                const int64_t gi = (b * p.L + gt) * p.D + d;
+                const bool ok = item_lane && dvalid && gt < p.L;
+                const float SA = sab[2 * i] * MMB_LN2;
+                const float SB = sab[2 * i + 1];
+                const float xv = xi[i];
+                if (HAS_Z) {
+                    const float zv = sz[tt * RP + dl];
+                    const float sg = sigmoid_f(zv);
+                    const float yfull = fmaf(Dv, xv, yv[i]);
+                    const float gz = sdo[tt * RP + dl] * yfull * sg * (1.f + zv * (1.f - sg));
+                    if (ok && gdz) E::store(gdz, gi, gz);
+                }
+                float gdt = fmaf(alpha * xv, SB, SA);
+                if (SOFTPLUS) gdt *= softplus_grad(ri[i]);
+                if (ok) {
+                    E::store(gdx, gi, fmaf(dyi[i], Dv, alpha * dti[i] * SB));
+                    E::store(gddl, gi, gdt);
+                    accD = fmaf(dyi[i], xv, accD);
+                    accBias += gdt;
+                }
+            }
+            __syncwarp();
+            // d-sum of this warp's rows of the window buffer (its DPW channels)
+            {
+                constexpr int ITEMS = MM_CK * NQ;
+                constexpr int IPT = ITEMS >= 32 ? ITEMS / 32 : 1;
+                constexpr int TPI = ITEMS >= 32 ? 1 : 32 / ITEMS;
+                constexpr int RPT = DPW / TPI > 0 ? DPW / TPI : 1;
+#pragma unroll
+                for (int j = 0; j < IPT; ++j) {
+                    const int item = (lane / TPI) + j * (32 / TPI), part = lane % TPI;
+                    const int s = item / NQ, q = item % NQ;
+                    float2 acc01 = f2(0.f), acc23 = f2(0.f);
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) {
+                        const int row = warp * DPW + part * RPT + r;
+                        const float4 vv = reinterpret_cast<const float4*>(
+                            wbuf + (s * DT + row) * 2 * N)[q ^ ((row & 1) ? SWZ : 0)];
+                        acc01 = fadd2(acc01, make_float2(vv.x, vv.y));
+                        acc23 = fadd2(acc23, make_float2(vv.z, vv.w));
+                    }
+#pragma unroll
+                    for (int m = 1; m < TPI; m <<= 1) {
+                        acc01.x += __shfl_xor_sync(FULL, acc01.x, m);
+                        acc01.y += __shfl_xor_sync(FULL, acc01.y, m);
+                        acc23.x += __shfl_xor_sync(FULL, acc23.x, m);
+                        acc23.y += __shfl_xor_sync(FULL, acc23.y, m);
+                    }
+                    const int64_t gt = t0 + w0 + s;
+                    if (part == 0 && gt < p.L) {
+                        const int col = q * 4;
+                        float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
+                        red_add_v4(dst, acc01.x, acc01.y, acc23.x, acc23.y);
+                    }
+                }
+            }
+            __syncwarp();
+        }
+        __syncthreads();
+    }
+
+    if (p.gstate_out && dvalid) {
+        // (a_0 gh_0, gv_0): an holds a of the first step now
+        float2 lam[NP2];
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) lam[j] = fmul2(an[j], gh[j]);
+        float* o = p.gstate_out + (b * p.D + d) * (2 * N) + ng * NP;
+        st_pairs_g<NP>(o, lam);
+        st_pairs_g<NP>(o + N, gv);
+    }
+    // dA: this thread's states of channel d, summed over its sequence
+    if (dvalid) {
+        float* dst = p.dA + d * N + ng * NP;
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) {
+            atomicAdd(dst + 2 * j, dA[j].x);
+            atomicAdd(dst + 2 * j + 1, dA[j].y);
+        }
+    }
+    // dD, dbias: sum the channel's lanes
+    accD = lane_sum<0, Cf::LOG2G>(accD);
+    accBias = lane_sum<0, Cf::LOG2G>(accBias);
+    if (ng == 0 && dvalid) {
+        if (p.dD) atomicAdd(p.dD + d, accD);
+        if (p.ddbias) atomicAdd(p.ddbias + d, accBias);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// backward segment summary: the adjoint pair leaving the first step when none
+// arrives from after the last one, (lam^0, mu^0) = (a_0 gh_0, gv_0).  Needs
+// only delta (for a), z and dout (for dy) and C; a reverse sweep without the
+// forward replay.
+// ---------------------------------------------------------------------------
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E>
+__global__ void __launch_bounds__(MM_NT) mmscan_bwd_summary_kernel(const MMParams p) {
+    using Cf = MMCfg<N, NP>;
+    using Sm = MMSmem<N, NP, 4, E::BYTES>;
+    using ET = typename E::T;
+    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, RP = Cf::RP, IPL = Cf::IPL, LB = Cf::LB;
+    constexpr int NP2 = Cf::NP2, TR = Cf::TR;
+    extern __shared__ float4 smem4[];
+    // same tile layout as the backward; x and B are not staged
+    MMStager<N, NP, 4, E> stg{reinterpret_cast<float*>(smem4), (int)threadIdx.x, 0, p.vec};
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ng = lane & (G - 1);
+    const int lane_base = lane & ~(G - 1);
+    const int ibase = rs_index<MM_CK, LB>(ng & ((1 << LB) - 1), 0);
+    const int dl = warp * Cf::DPW + (lane >> Cf::LOG2G);
+    const int64_t b = blockIdx.y;
+    const int64_t d0 = (int64_t)blockIdx.x * DT;
+    const int64_t d = d0 + dl;
+    const bool dvalid = d < p.D;
+    stg.dcols = (int)min64(DT, p.D - d0);
+    const ET* gdl = static_cast<const ET*>(p.delta);
+    const ET* gz = static_cast<const ET*>(p.z);
+    const ET* gdo = static_cast<const ET*>(p.dout);
+    const ET* gC = static_cast<const ET*>(p.Cm);
+
+    float2 A2[NP2], gh[NP2], gv[NP2], an[NP2];
+#pragma unroll
+    for (int j = 0; j < NP2; ++j) {
+        A2[j] = gh[j] = gv[j] = an[j] = f2(0.f);
+        if (dvalid) {
+            const float* Ar = p.A + d * N + ng * NP + 2 * j;
+            A2[j] = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
+        }
+    }
+    const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
+    const float2 beta2 = f2(p.beta);
+    const int nchunks = (int)((p.L + T - 1) / T);
+
+    auto stage = [&](int slot, int c) {
+        const int64_t t0 = (int64_t)c * T;
+        const int rv = (int)min64(T, p.L - t0);
+        stg.tile_d(slot, 1, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1], rv);
+        if (HAS_Z) stg.tile_d(slot, 2, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1], rv);
+        stg.tile_d(slot, 3, gdo + (b * p.L + t0) * p.D + d0, p.D, rv);
+        stg.tile_n(slot, 1, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
+    };
+    constexpr unsigned DMASK = HAS_Z ? 14u : 10u;
+
+#pragma unroll
+    for (int it = 0; it < MM_NS - 1; ++it) {
+        if (it < nchunks) stage(it, nchunks - 1 - it);
+        cp_async_commit();
+    }
+    for (int it = 0; it < nchunks; ++it) {
+        const int c = nchunks - 1 - it;
+        if (it + MM_NS - 1 < nchunks) stage((it + MM_NS - 1) % MM_NS, c - (MM_NS - 1));
+        cp_async_commit();
+        cp_async_wait<MM_NS - 1>();
+        __syncthreads();
+        const float* st = stg.view(it % MM_NS, DMASK, 2u);
+        if (Sm::WIDE) __syncthreads();
+        const float* sdl = st + TR;
+        const float* sz = st + 2 * TR;
+        const float* sdo = st + 3 * TR;
+        const float* sC = st + 4 * TR + Cf::TN;
+        const int64_t t0 = (int64_t)c * T;
+        const int Lc = (int)min64(T, p.L - t0);
+
+        for (int w = (Lc - 1) / MM_CK; w >= 0; --w) {
+            const int w0 = w * MM_CK;
+            float dti[IPL], dyi[IPL];
+#pragma unroll
+            for (int i = 0; i < IPL; ++i) {
+                const int row = (w0 + ibase + i) * RP + dl;
+                const float r = sdl[row] + bias_d;
+                dti[i] = SOFTPLUS ? softplus_f(r) : r;
+                float dy = sdo[row];
+                if (HAS_Z) {
+                    const float zv = sz[row];
+                    dy *= zv * sigmoid_f(zv);
+                }
+                dyi[i] = dy;
+            }
+            float dts[MM_CK], dys[MM_CK];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+                const int src = lane_base | block_owner<LB>(s - s % IPL);
+                dts[s] = __shfl_sync(FULL, dti[s % IPL], src);
+                dys[s] = __shfl_sync(FULL, dyi[s % IPL], src);
+            }
+            float2 aa[MM_CK][NP2];
+#pragma unroll
+            for (int s = 0; s < MM_CK; ++s) {
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    const float2 e = fmul2(f2(dts[s]), A2[j]);
+                    aa[s][j] = make_float2(ex2(e.x), ex2(e.y));
+                }
+            }
+#pragma unroll
+            for (int s = MM_CK - 1; s >= 0; --s) {
+                float2 cq[NP2];
+                ld_pairs<NP>(sC + (w0 + s) * N + ng * NP, cq);
+                const float2 dy2 = f2(dys[s]);
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    gh[j] = ffma2(an[j], gh[j], fmul2(dy2, cq[j]));
+                    gv[j] = ffma2(beta2, gv[j], gh[j]);
+                    an[j] = aa[s][j];
+                }
+            }
+        }
+        __syncthreads();
+    }
+    if (!dvalid) return;
+    float2 lam[NP2];
+#pragma unroll
+    for (int j = 0; j < NP2; ++j) lam[j] = fmul2(an[j], gh[j]);
+    float* o = p.summary + (b * p.D + d) * (2 * N) + ng * NP;
+    st_pairs_g<NP>(o, lam);
+    st_pairs_g<NP>(o + N, gv);
+}
+
+// ---------------------------------------------------------------------------
+// host-side launchers (instantiated per element type in separate units)
+// ---------------------------------------------------------------------------
+template <int N, int NP, bool SP, bool Z, class E, bool SUMM>
+int launch_fwd_t(const MMParams& p, cudaStream_t stream) {
+    using Cf = MMCfg<N, NP>;
+    const size_t smem = sizeof(float) * MMSmem<N, NP, 3, E::BYTES>::FLOATS;
+    static int attr_done[MMB_MAX_DEVICES] = {};
+    const int st = mmb_smem_attr(mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM>, smem, attr_done);
+    if (st != MMB_OK) return st;
+    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
+    mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM><<<grid, MM_NT, smem, stream>>>(p);
+    return mmb_launch_status();
+}
+
+template <int N, int NP, bool SP, bool Z, class E>
+int launch_bwd_t(const MMParams& p, cudaStream_t stream) {
+    using Cf = MMCfg<N, NP>;
+    const size_t smem =
+        sizeof(float) * (MMSmem<N, NP, 4, E::BYTES>::FLOATS + MM_CK * Cf::DT * 2 * N);
+    static int attr_done[MMB_MAX_DEVICES] = {};
+    const int st = mmb_smem_attr(mmscan_bwd_kernel<N, NP, SP, Z, E>, smem, attr_done);
+    if (st != MMB_OK) return st;
+    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
+    mmscan_bwd_kernel<N, NP, SP, Z, E><<<grid, MM_NT, smem, stream>>>(p);
+    return mmb_launch_status();
+}
+
+template <int N, int NP, bool SP, bool Z, class E>
+int launch_bwd_summary_t(const MMParams& p, cudaStream_t stream) {
+    using Cf = MMCfg<N, NP>;
+    const size_t smem = sizeof(float) * MMSmem<N, NP, 4, E::BYTES>::FLOATS;
+    static int attr_done[MMB_MAX_DEVICES] = {};
+    const int st = mmb_smem_attr(mmscan_bwd_summary_kernel<N, NP, SP, Z, E>, smem, attr_done);
+    if (st != MMB_OK) return st;
+    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
+    mmscan_bwd_summary_kernel<N, NP, SP, Z, E><<<grid, MM_NT, smem, stream>>>(p);
+    return mmb_launch_status();
+}
+
+// What a launch computes.
+enum MMKind { MM_FWD = 0, MM_FWD_SUMMARY = 1, MM_BWD = 2, MM_BWD_SUMMARY = 3 };
+
+// forward side (MM_FWD, MM_FWD_SUMMARY) or backward side (MM_BWD, MM_BWD_SUMMARY)
+template <int N, int NP, class E, bool FWDSIDE>
+int launch_side(const MMParams& p, int kind, cudaStream_t s) {
+    const bool z = p.z != nullptr;
+    const bool sp = p.softplus != 0;
+    if constexpr (FWDSIDE) {
+        if (kind == MM_FWD_SUMMARY)
+            return sp ? launch_fwd_t<N, NP, true, false, E, true>(p, s)
+                      : launch_fwd_t<N, NP, false, false, E, true>(p, s);
+        if (sp) return z ? launch_fwd_t<N, NP, true, true, E, false>(p, s)
+                         : launch_fwd_t<N, NP, true, false, E, false>(p, s);
+        return z ? launch_fwd_t<N, NP, false, true, E, false>(p, s)
+                 : launch_fwd_t<N, NP, false, false, E, false>(p, s);
+    } else {
+        if (kind == MM_BWD_SUMMARY) {
+            if (sp) return z ? launch_bwd_summary_t<N, NP, true, true, E>(p, s)
+                             : launch_bwd_summary_t<N, NP, true, false, E>(p, s);
+            return z ? launch_bwd_summary_t<N, NP, false, true, E>(p, s)
+                     : launch_bwd_summary_t<N, NP, false, false, E>(p, s);
+        }
+        if (sp) return z ? launch_bwd_t<N, NP, true, true, E>(p, s)
+                         : launch_bwd_t<N, NP, true, false, E>(p, s);
+        return z ? launch_bwd_t<N, NP, false, true, E>(p, s)
+                 : launch_bwd_t<N, NP, false, false, E>(p, s);
+    }
+}
+
+// bf16 calls always use 4 states per thread (their shapes are large).
+template <int N, class E, bool FWDSIDE>
+int launch_np(const MMParams& p, int NP, int kind, cudaStream_t s) {
+    if constexpr (E::BYTES == 4 && N != 64) {
+        if (NP == 2) return launch_side<N, 2, E, FWDSIDE>(p, kind, s);
+    }
+    return launch_side<N, 4, E, FWDSIDE>(p, kind, s);
+}
+
+// Runtime (dstate, states per thread) -> template.  Explicitly instantiated
+// once per (element type, side) in mmscan_{f32,bf16}_{fwd,bwd}.cu so the four
+// kernel families compile in parallel.
+template <class E, bool FWDSIDE>
+int mmscan_launch(const MMParams& p, int64_t N, int NP, int kind, cudaStream_t s) {
+    switch (N) {
+        case 8: return launch_np<8, E, FWDSIDE>(p, NP, kind, s);
+        case 16: return launch_np<16, E, FWDSIDE>(p, NP, kind, s);
+        case 32: return launch_np<32, E, FWDSIDE>(p, NP, kind, s);
+        case 64: return launch_np<64, E, FWDSIDE>(p, NP, kind, s);
+        default: return MMB_ERR_UNSUPPORTED;
+    }
+}
+
+extern template int mmscan_launch<ElemF32, true>(const MMParams&, int64_t, int, int, cudaStream_t);
+extern template int mmscan_launch<ElemF32, false>(const MMParams&, int64_t, int, int, cudaStream_t);
+extern template int mmscan_launch<ElemBF16, true>(const MMParams&, int64_t, int, int, cudaStream_t);
+extern template int mmscan_launch<ElemBF16, false>(const MMParams&, int64_t, int, int, cudaStream_t);
+
+}  // namespace mmb

@@ -50,10 +50,13 @@ def _load():
         lib = ctypes.CDLL(_LIB_PATH)
         for sfx in ("f64", "f32"):
             getattr(lib, f"orc_mmscan_fwd_{sfx}").argtypes = (
-                [_i64] * 4 + [_ptr] * 8 + [ctypes.c_int, ctypes.c_double, ctypes.c_double, _ptr, _ptr])
+                [_i64] * 4 + [_ptr] * 8 + [ctypes.c_int, ctypes.c_double, ctypes.c_double]
+                + [_ptr] * 4)
+            getattr(lib, f"orc_mmscan_fwd_summary_{sfx}").argtypes = (
+                [_i64] * 4 + [_ptr] * 5 + [ctypes.c_int, ctypes.c_double, ctypes.c_double, _ptr])
             getattr(lib, f"orc_mmscan_bwd_{sfx}").argtypes = (
                 [_i64] * 4 + [_ptr] * 8 + [ctypes.c_int, ctypes.c_double, ctypes.c_double]
-                + [_ptr] * 9)
+                + [_ptr] * 12)
             getattr(lib, f"orc_rows_fwd_{sfx}").argtypes = [
                 _i64, _i64, _ptr, ctypes.c_double, _ptr, _ptr, _ptr]
             getattr(lib, f"orc_rows_bwd_{sfx}").argtypes = [
@@ -97,27 +100,56 @@ def _p(a):
 # momentum selective scan  (mamba_momentum.py:256-323 + gating :227-229)
 # ---------------------------------------------------------------------------
 def mmscan_fwd(x, delta, A, B, C, D=None, z=None, delta_bias=None, delta_softplus=False,
-               beta=0.6, alpha=1.0, prec="f64", return_ypre=False):
-    """y = selective momentum scan; shapes x/delta/z (Bsz,L,Dm), A (Dm,N), B/C (Bsz,L,N)."""
+               beta=0.6, alpha=1.0, prec="f64", return_ypre=False, state_in=None,
+               return_state=False):
+    """y = selective momentum scan; shapes x/delta/z (Bsz,L,Dm), A (Dm,N), B/C (Bsz,L,N).
+
+    state_in (Bsz, Dm, 2, N) = (h, v) before the first step (zeros when None);
+    return_state adds the state after the last step, same layout."""
     dt = _dt(prec)
     x, delta, A, B, C = (_c(t, dt) for t in (x, delta, A, B, C))
-    D, z, delta_bias = _c(D, dt), _c(z, dt), _c(delta_bias, dt)
+    D, z, delta_bias, state_in = _c(D, dt), _c(z, dt), _c(delta_bias, dt), _c(state_in, dt)
     Bsz, L, Dm = x.shape
     N = A.shape[1]
     out = np.empty_like(x)
     ypre = np.empty_like(x) if return_ypre else None
+    state_out = np.empty((Bsz, Dm, 2, N), dt) if return_state else None
     getattr(_load(), f"orc_mmscan_fwd_{prec}")(
         Bsz, L, Dm, N, _p(x), _p(delta), _p(A), _p(B), _p(C), _p(D), _p(z), _p(delta_bias),
-        int(bool(delta_softplus)), float(beta), float(alpha), _p(out), _p(ypre))
-    return (out, ypre) if return_ypre else out
+        int(bool(delta_softplus)), float(beta), float(alpha), _p(out), _p(ypre),
+        _p(state_in), _p(state_out))
+    res = (out,) + ((ypre,) if return_ypre else ()) + ((state_out,) if return_state else ())
+    return res if len(res) > 1 else out
+
+
+def mmscan_fwd_summary(x, delta, A, B, delta_bias=None, delta_softplus=False, beta=0.6,
+                       alpha=1.0, prec="f64"):
+    """Segment summary (Bsz, Dm, 4, N) = [h^0 | v^0 | P | Q']: the segment's end state
+    from a zero state and its transition, h_T = P h_0 + beta Q' v_0 + h^0,
+    v_T = beta^T v_0 + v^0."""
+    dt = _dt(prec)
+    x, delta, A, B = (_c(t, dt) for t in (x, delta, A, B))
+    delta_bias = _c(delta_bias, dt)
+    Bsz, L, Dm = x.shape
+    N = A.shape[1]
+    summ = np.empty((Bsz, Dm, 4, N), dt)
+    getattr(_load(), f"orc_mmscan_fwd_summary_{prec}")(
+        Bsz, L, Dm, N, _p(x), _p(delta), _p(A), _p(B), _p(delta_bias),
+        int(bool(delta_softplus)), float(beta), float(alpha), _p(summ))
+    return summ
 
 
 def mmscan_bwd(x, delta, A, B, C, D, z, delta_bias, delta_softplus, beta, alpha, dout,
-               prec="f64"):
-    """Gradients (dx, ddelta, dA, dB, dC, dD, dz, ddelta_bias); absent inputs give None."""
+               prec="f64", state_in=None, gstate_in=None, return_gstate=False):
+    """Gradients (dx, ddelta, dA, dB, dC, dD, dz, ddelta_bias); absent inputs give None.
+
+    For one segment of a split sequence: state_in as given to the forward,
+    gstate_in (Bsz, Dm, 2, N) = (a gh, gv) arriving from the step after the
+    segment; return_gstate appends the same pair leaving its first step."""
     dt = _dt(prec)
     x, delta, A, B, C, dout = (_c(t, dt) for t in (x, delta, A, B, C, dout))
     D, z, delta_bias = _c(D, dt), _c(z, dt), _c(delta_bias, dt)
+    state_in, gstate_in = _c(state_in, dt), _c(gstate_in, dt)
     Bsz, L, Dm = x.shape
     N = A.shape[1]
     dx, ddelta = np.empty_like(x), np.empty_like(x)
@@ -126,11 +158,14 @@ def mmscan_bwd(x, delta, A, B, C, D, z, delta_bias, delta_softplus, beta, alpha,
     dD = np.empty((Dm,), dt) if D is not None else None
     dz = np.empty_like(x) if z is not None else None
     ddb = np.empty((Dm,), dt) if delta_bias is not None else None
+    gout = np.empty((Bsz, Dm, 2, N), dt) if return_gstate else None
     getattr(_load(), f"orc_mmscan_bwd_{prec}")(
         Bsz, L, Dm, N, _p(x), _p(delta), _p(A), _p(B), _p(C), _p(D), _p(z), _p(delta_bias),
         int(bool(delta_softplus)), float(beta), float(alpha), _p(dout),
-        _p(dx), _p(ddelta), _p(dA), _p(dB), _p(dC), _p(dD), _p(dz), _p(ddb))
-    return dx, ddelta, dA, dB, dC, dD, dz, ddb
+        _p(dx), _p(ddelta), _p(dA), _p(dB), _p(dC), _p(dD), _p(dz), _p(ddb),
+        _p(state_in), _p(gstate_in), _p(gout))
+    res = (dx, ddelta, dA, dB, dC, dD, dz, ddb)
+    return res + (gout,) if return_gstate else res
 
 
 # ---------------------------------------------------------------------------

@@ -28,18 +28,24 @@ static inline REAL SFX(sigmoid_)(REAL r) { return (REAL)1 / ((REAL)1 + EXP(-r));
  *   y    = sum_n C[n]*h + D*x                           (mamba_momentum.py:319-321)
  *   out  = y * silu(z)  when z is given                 (mamba_momentum.py:227-229)
  * ypre (nullable) receives y before the gate.
+ * state_in / state_out (nullable, (Bsz, D, 2, N): h then v) are the state
+ * before the first step (zeros when NULL) and after the last one; they carry
+ * a sequence split into consecutive segments from one segment to the next.
  * ------------------------------------------------------------------------- */
 void SFX(orc_mmscan_fwd)(i64 Bsz, i64 L, i64 D, i64 N,
                          const REAL* x, const REAL* delta, const REAL* A,
                          const REAL* Bm, const REAL* Cm, const REAL* Dskip,
                          const REAL* z, const REAL* dbias, int softplus,
-                         double beta_d, double alpha_d, REAL* out, REAL* ypre) {
+                         double beta_d, double alpha_d, REAL* out, REAL* ypre,
+                         const REAL* state_in, REAL* state_out) {
     const REAL beta = (REAL)beta_d, alpha = (REAL)alpha_d;
 #pragma omp parallel for schedule(dynamic, 4)
     for (i64 bd = 0; bd < Bsz * D; ++bd) {
         const i64 b = bd / D, d = bd % D;
         REAL* h = (REAL*)calloc((size_t)(2 * N), sizeof(REAL));
         REAL* v = h + N;
+        if (state_in)
+            for (i64 n = 0; n < 2 * N; ++n) h[n] = state_in[bd * 2 * N + n];
         for (i64 t = 0; t < L; ++t) {
             const i64 io = (b * L + t) * D + d;
             const i64 bo = (b * L + t) * N;
@@ -63,7 +69,51 @@ void SFX(orc_mmscan_fwd)(i64 Bsz, i64 L, i64 D, i64 N,
             }
             out[io] = y;
         }
+        if (state_out)
+            for (i64 n = 0; n < 2 * N; ++n) state_out[bd * 2 * N + n] = h[n];
         free(h);
+    }
+}
+
+/* ---------------------------------------------------------------------------
+ * Segment summary of the forward recurrence, for a sequence split into
+ * consecutive segments.  Over one segment of T steps the state maps as
+ *   h_T = P h_0 + beta Q' v_0 + h_T^0 ;  v_T = beta^T v_0 + v_T^0
+ * with (h^0, v^0) the segment's result from a zero state, P = prod_t a_t and
+ * Q' = sum_{t=1..T} beta^{t-1} prod_{s>t} a_s (Q'_t = a_t Q'_{t-1} + beta^{t-1}).
+ * summary: (Bsz, D, 4, N) = [h^0 | v^0 | P | Q'].
+ * ------------------------------------------------------------------------- */
+void SFX(orc_mmscan_fwd_summary)(i64 Bsz, i64 L, i64 D, i64 N,
+                                 const REAL* x, const REAL* delta, const REAL* A,
+                                 const REAL* Bm, const REAL* dbias, int softplus,
+                                 double beta_d, double alpha_d, REAL* summary) {
+    const REAL beta = (REAL)beta_d, alpha = (REAL)alpha_d;
+#pragma omp parallel for schedule(dynamic, 4)
+    for (i64 bd = 0; bd < Bsz * D; ++bd) {
+        const i64 b = bd / D, d = bd % D;
+        REAL* h = summary + bd * 4 * N;
+        REAL* v = h + N;
+        REAL* P = h + 2 * N;
+        REAL* Q = h + 3 * N;
+        for (i64 n = 0; n < N; ++n) { h[n] = 0; v[n] = 0; P[n] = 1; Q[n] = 0; }
+        REAL bp = 1; /* beta^(t-1) */
+        for (i64 t = 0; t < L; ++t) {
+            const i64 io = (b * L + t) * D + d;
+            const i64 bo = (b * L + t) * N;
+            REAL dt = delta[io];
+            if (dbias) dt += dbias[d];
+            if (softplus) dt = SFX(softplus_)(dt);
+            const REAL xv = x[io];
+            for (i64 n = 0; n < N; ++n) {
+                const REAL a = EXP(dt * A[d * N + n]);
+                const REAL u = alpha * (dt * Bm[bo + n]) * xv;
+                v[n] = beta * v[n] + u;
+                h[n] = a * h[n] + v[n];
+                P[n] = a * P[n];
+                Q[n] = a * Q[n] + bp;
+            }
+            bp *= beta;
+        }
     }
 }
 
@@ -73,7 +123,10 @@ void SFX(orc_mmscan_fwd)(i64 Bsz, i64 L, i64 D, i64 N,
  *   du_t = gv_t;   da_t = gh_t*h_{t-1} (zero at t = 0, as pscan.py:229-230 and
  *   momentum_scan_cuda.py:77 leave it)
  * Every output is overwritten.  dz / ddbias / dD may be NULL when the matching
- * input was absent.  Parallel over (b, block of 8 channels); the d-sums of dB
+ * input was absent.
+ * Segments (all nullable, (Bsz, D, 2, N)): state_in is the forward's state_in;
+ * gstate_in = (a_L gh_L, gv_L) arriving from the step after the segment (zeros
+ * when NULL), gstate_out = (a_0 gh_0, gv_0) leaving it towards the step before.  Parallel over (b, block of 8 channels); the d-sums of dB
  * and dC and the (b,t)-sums of dA/dD/ddbias are reduced in a fixed order.
  * ------------------------------------------------------------------------- */
 void SFX(orc_mmscan_bwd)(i64 Bsz, i64 L, i64 D, i64 N,
@@ -82,7 +135,8 @@ void SFX(orc_mmscan_bwd)(i64 Bsz, i64 L, i64 D, i64 N,
                          const REAL* z, const REAL* dbias, int softplus,
                          double beta_d, double alpha_d, const REAL* dout,
                          REAL* dx, REAL* ddelta, REAL* dA, REAL* dB, REAL* dC,
-                         REAL* dD, REAL* dz, REAL* ddbias) {
+                         REAL* dD, REAL* dz, REAL* ddbias, const REAL* state_in,
+                         const REAL* gstate_in, REAL* gstate_out) {
     const REAL beta = (REAL)beta_d, alpha = (REAL)alpha_d;
     const i64 DB = 8;
     const i64 nblk = (D + DB - 1) / DB;
@@ -107,7 +161,11 @@ void SFX(orc_mmscan_bwd)(i64 Bsz, i64 L, i64 D, i64 N,
         for (i64 d = blk * DB; d < D && d < (blk + 1) * DB; ++d) {
             /* forward replay; hs[t+1] holds h_t, hs[0] = 0 */
             REAL* v = gv; /* reuse as forward momentum state */
-            for (i64 n = 0; n < N; ++n) { hs[n] = 0; v[n] = 0; }
+            const i64 so = (b * D + d) * 2 * N;
+            for (i64 n = 0; n < N; ++n) {
+                hs[n] = state_in ? state_in[so + n] : (REAL)0;
+                v[n] = state_in ? state_in[so + N + n] : (REAL)0;
+            }
             for (i64 t = 0; t < L; ++t) {
                 const i64 io = (b * L + t) * D + d;
                 const i64 bo = (b * L + t) * N;
@@ -128,10 +186,15 @@ void SFX(orc_mmscan_bwd)(i64 Bsz, i64 L, i64 D, i64 N,
                 if (Dskip) y += Dskip[d] * xv;
                 yp[t] = y;
             }
-            for (i64 n = 0; n < N; ++n) { gh[n] = 0; gv[n] = 0; }
             REAL accD = 0, accBias = 0;
-            /* a_{t+1} factors carried from the previous (later) step */
+            /* a_{t+1} factors carried from the previous (later) step; a carry
+               arriving from the right enters as gh = a_L gh_L with a factor 1 */
             REAL* anext = (REAL*)calloc((size_t)N, sizeof(REAL));
+            for (i64 n = 0; n < N; ++n) {
+                gh[n] = gstate_in ? gstate_in[so + n] : (REAL)0;
+                gv[n] = gstate_in ? gstate_in[so + N + n] : (REAL)0;
+                anext[n] = gstate_in ? (REAL)1 : (REAL)0;
+            }
             for (i64 t = L - 1; t >= 0; --t) {
                 const i64 io = (b * L + t) * D + d;
                 const i64 bo = (b * L + t) * N;
@@ -158,7 +221,7 @@ void SFX(orc_mmscan_bwd)(i64 Bsz, i64 L, i64 D, i64 N,
                     tB[t * N + n] += du * alpha * dt * xv;
                     gx += du * alpha * dt * Bm[bo + n];
                     gdt += du * alpha * Bm[bo + n] * xv;
-                    const REAL da = gh[n] * hprev; /* hprev = 0 at t = 0 */
+                    const REAL da = gh[n] * hprev; /* hprev = state_in (0) at t = 0 */
                     gdt += da * a * A[d * N + n];
                     pA[(b * D + d) * N + n] += da * a * dt;
                     anext[n] = a;
@@ -171,6 +234,11 @@ void SFX(orc_mmscan_bwd)(i64 Bsz, i64 L, i64 D, i64 N,
                 ddelta[io] = gdt;
                 accBias += gdt;
             }
+            if (gstate_out)
+                for (i64 n = 0; n < N; ++n) {
+                    gstate_out[so + n] = anext[n] * gh[n];
+                    gstate_out[so + N + n] = gv[n];
+                }
             free(anext);
             pD[b * D + d] = accD;
             pbias[b * D + d] = accBias;
