@@ -270,11 +270,11 @@ def run_b200(args):
     torch.cuda.synchronize()
 
     sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
-    barrier()
-    torch.cuda.synchronize()
-    if sampler:
+    if sampler:  # before the barrier, so that every rank starts the timed steps together
         sampler.start()
         time.sleep(0.5)
+    barrier()
+    torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -447,7 +447,7 @@ def cpu_baseline(budget_s=15.0):
     while True:
         cpu_scan_layer(oracle, inp)
         n += 1
-        if time.perf_counter() - t0 >= budget_s or n >= 64:
+        if time.perf_counter() - t0 >= budget_s:
             break
     dt = time.perf_counter() - t0
     elems = n * nseq * SEQ * DIM * DST
@@ -496,6 +496,152 @@ def run_reference(args):
     }
 
 
+# ---------------------------------------------------------------------------
+# long-sequence workload: one sequence split along time across the ranks
+# ---------------------------------------------------------------------------
+LONG = dict(batch=8, seqlen=65536, dim=2048, dstate=16, beta=0.9, alpha=1.0)
+
+
+def long_bytes(Bsz, L, D, N):
+    """Algorithmic bytes of one fwd+bwd over (Bsz, L) with bf16 activations:
+    fwd reads x, delta, B, C and writes y; bwd reads x, delta, B, C, dy and
+    writes dx, ddelta, dB, dC (fp32 sums counted at 4 bytes)."""
+    fwd = 2 * (3 * Bsz * L * D + 2 * Bsz * L * N) + 4 * (D * N + D)
+    bwd = 2 * (5 * Bsz * L * D + 2 * Bsz * L * N) + 4 * (2 * Bsz * L * N + 2 * D * N + 2 * D)
+    return fwd, bwd
+
+
+def run_long(args):
+    """B=8, L=65536, D=2048, N=16 with bf16 activations, fp32 state: the
+    sequence is split into WORLD_SIZE contiguous segments, one per rank
+    (segment summaries all-gathered over NCCL, carries folded locally).  Total
+    work is fixed (strong scaling)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from momentummamba_b200.selective_scan import ScanCall
+    from momentummamba_b200.seqshard import SegmentOps as ops
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    Bsz, L, D, N = (LONG[k] for k in ("batch", "seqlen", "dim", "dstate"))
+    beta, alpha = LONG["beta"], LONG["alpha"]
+    Lr = L // world
+    seg_lens = [Lr] * world
+    gen = torch.Generator(device=dev).manual_seed(77 + rank)
+    bf = torch.bfloat16
+    x = torch.randn(Bsz, Lr, D, device=dev, generator=gen).to(bf)
+    delta = torch.nn.functional.softplus(
+        0.5 * torch.randn(Bsz, Lr, D, device=dev, generator=gen) - 2.0).to(bf)
+    Bm = torch.randn(Bsz, Lr, N, device=dev, generator=gen).to(bf)
+    Cm = torch.randn(Bsz, Lr, N, device=dev, generator=gen).to(bf)
+    A = -torch.arange(1, N + 1, device=dev, dtype=torch.float32).repeat(D, 1)
+    Dk = torch.ones(D, device=dev)
+    dout = torch.randn(Bsz, Lr, D, device=dev, generator=gen).to(bf)
+    call = ScanCall(x, delta, A, Bm, Cm, Dk, None, None, False, beta, alpha)
+    assert call.adtype == bf
+
+    def gather(t):
+        out = torch.empty((world * t.shape[0],) + tuple(t.shape[1:]), device=dev)
+        dist.all_gather_into_tensor(out, t)
+        return out.view((world,) + tuple(t.shape))
+
+    marks = {}
+
+    def mark(name):
+        if args.phases:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            marks.setdefault(name, []).append(e)
+
+    def step():
+        mark("start")
+        if world > 1:
+            summ = gather(ops.fwd_summary(call))
+            state = ops.carry_fwd(summ, rank, seg_lens, beta) if rank > 0 else None
+        else:
+            summ, state = None, None
+        mark("fwd_carry")
+        _, ckpt = ops.forward(call, state, True)
+        mark("fwd")
+        gstate = None
+        if world > 1:
+            gs = ops.bwd_summary(call, dout)
+            gsumm = gather(gs)
+            gstate = ops.carry_bwd(summ, gsumm, rank, seg_lens, beta) if rank < world - 1 else None
+        mark("bwd_carry")
+        g = ops.backward(call, ckpt, dout, gstate)
+        if world > 1:
+            flat = torch.cat([g[2].reshape(-1), g[5]])
+            dist.all_reduce(flat)
+        mark("bwd")
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    marks.clear()
+    sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
+    if sampler:  # before the barrier, so that every rank starts the timed steps together
+        sampler.start()
+        time.sleep(0.5)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        step()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    phases = None
+    if args.phases and marks:
+        names = ["start", "fwd_carry", "fwd", "bwd_carry", "bwd"]
+        phases = {}
+        for a, b in zip(names[:-1], names[1:]):
+            t = statistics.mean(marks[a][i].elapsed_time(marks[b][i]) for i in range(args.steps))
+            phases[b] = max_over_ranks(t, world, dev)
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    elems = Bsz * L * D * N
+    fb, bb = long_bytes(Bsz, Lr, D, N)
+    peak, peak_kind = load_peaks()
+    ms_step = ms / args.steps
+    achieved = (fb + bb) / (ms_step / 1e3) / 1e9  # per GPU: its segment's bytes over the step
+    return {
+        "metric": METRIC, "value": elems / (ms_step / 1e3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic",
+        "config": {"workload": "long-sequence scan fwd+bwd: B=8 L=65536 D=2048 N=16, bf16 "
+                               "activations, fp32 state; x ~ N(0,1), delta = softplus(0.5 N(0,1) - 2), "
+                               "A[d,n] = -(n+1), D = 1, beta 0.9, alpha 1",
+                   "parallelism": f"sequence-sharded x{world} (segment summaries all-gathered)",
+                   "segment": Lr, "l2": "inputs larger than L2 (2.1 GB per bf16 activation)"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": achieved / peak,
+                     "algorithmic_bytes_per_gpu_step": fb + bb, "traffic": None,
+                     "scope": "whole step per GPU (fwd+bwd kernels, carries, collectives)"},
+        "phases_ms": phases,
+        # rank 0: forward, backward; with segments also both summaries and the adjoint fold
+        "gpu_launches": (2 if world == 1 else 5) * args.steps,
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -510,9 +656,19 @@ def main():
                     help="run warm-up and steps eagerly and exit (for profiler captures)")
     ap.add_argument("--batch", type=int, default=BSZ,
                     help="sequences per layer (profiling only; the benchmark line uses 32)")
+    ap.add_argument("--workload", choices=["stack", "long"], default="stack",
+                    help="stack: the 4-layer MambaMomentum scan (batch-sharded, the benchmark "
+                         "line); long: B=8 L=65536 D=2048 bf16, sequence-sharded")
+    ap.add_argument("--phases", action="store_true",
+                    help="long workload: also time each phase (adds events to the step)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
-    line = run_reference(args) if args.impl == "reference" else run_b200(args)
+    if args.impl == "reference":
+        line = run_reference(args)
+    elif args.workload == "long":
+        line = run_long(args)
+    else:
+        line = run_b200(args)
     if line is not None:
         print(json.dumps(line), flush=True)
 
