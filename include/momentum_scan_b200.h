@@ -198,6 +198,65 @@ int mmb_mmscan_carry_bwd(int64_t nseg, int64_t seg, const int64_t* seg_len, int6
                          const float* gsummaries, float* gstate_in, mmb_stream_t stream);
 
 /* =========================================================================
+ * The block's producer: causal depthwise conv1d + SiLU over time,
+ *   out[b,t,d] = silu(bias[d] + sum_k weight[d,k] x[b, t-(width-1)+k, d]),
+ * inputs before t = 0 from state_in (batch, dim, width-1) or zeros.
+ *   Replaces conv1d(x.transpose(1, 2))[:, :, :L] + silu of the block's x branch
+ *   (mamba_momentum.py:217-223; weight (dim, 1, width) of nn.Conv1d with
+ *   groups = dim, padding = width-1).
+ * x: (batch, seqlen, dim) with strides x_stride[0..1] (dim unit-stride);
+ * out, dout, dx: contiguous (batch, seqlen, dim); weight (dim, width); bias
+ * (dim) nullable; width 2..8.  state_out (nullable) receives the last width-1
+ * inputs (the decode cache).  The backward writes dx (no gradient reaches
+ * state_in) and the sums dweight (dim, width) and dbias (when bias given).
+ * ========================================================================= */
+int mmb_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t dim, int32_t width,
+                        const float* x, const int64_t* x_stride, const float* weight,
+                        const float* bias, const float* state_in, float* state_out,
+                        float* out, mmb_stream_t stream);
+
+int mmb_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t dim, int32_t width,
+                        const float* x, const int64_t* x_stride, const float* weight,
+                        const float* bias, const float* state_in, const float* dout,
+                        float* dx, float* dweight, float* dbias, mmb_stream_t stream);
+
+/* =========================================================================
+ * Decode (one token per call).
+ *
+ * mmb_conv1d_step: out = silu(bias + sum_k weight[:,k] [state_in | x][k]) and
+ * state_out = state_in (batch, dim, width-1) shifted left with x appended
+ * (mamba_momentum.py:455-459, :466); state_out may be state_in (in place).
+ * x rows x_row_stride apart.
+ *
+ * mmb_mmscan_step: the single-token momentum update (mamba_momentum.py:473-515)
+ * with the block's softplus and gate fused:
+ *   dt = softplus(delta + delta_bias) or delta; a = exp(dt A)
+ *   v = beta v + alpha dt B x ;  h = a h + v ;  out = (C.h + D x) * silu(z)
+ * h_in, v_in (element (b, d, n) at b*state_stride[0] + d*state_stride[1] + n;
+ * NULL = zero state, the reference's None cache) give the state before the
+ * token and h, v (same layout; may be h_in, v_in) receive it after: the
+ * reference's (batch, dim, dstate) caches, or the h and v halves of a
+ * forward's state_out.  D, z, delta_bias nullable.
+ * ========================================================================= */
+typedef struct mmb_step_desc {
+    int64_t batch, dim, dstate;
+    int64_t x_row_stride, delta_row_stride, z_row_stride, B_row_stride, C_row_stride;
+    int64_t state_stride[2];
+    float beta, alpha;
+    int32_t delta_softplus;
+    int32_t reserved;
+} mmb_step_desc;
+
+int mmb_conv1d_step(int64_t batch, int64_t dim, int32_t width, const float* x,
+                    int64_t x_row_stride, const float* state_in, float* state_out,
+                    const float* weight, const float* bias, float* out, mmb_stream_t stream);
+
+int mmb_mmscan_step(const mmb_step_desc* desc, const float* x, const float* delta,
+                    const float* A, const float* B, const float* C, const float* D,
+                    const float* z, const float* delta_bias, const float* h_in,
+                    const float* v_in, float* h, float* v, float* out, mmb_stream_t stream);
+
+/* =========================================================================
  * Row scan:  v_t = beta*v_{t-1} + u_t ;  h_t = a_t*h_{t-1} + v_t  over the rows
  * of contiguous (rows, L) tensors (t unit-stride).
  *   Replaces momentum_scan_kernel / launch_forward (momentum_scan_cuda.py:22-47,

@@ -45,6 +45,16 @@ class MMScanTensors(ctypes.Structure):
         "ddelta_bias", "gstate_out")]
 
 
+class StepDesc(ctypes.Structure):
+    """mirror of struct mmb_step_desc"""
+    _fields_ = [
+        ("batch", _c_i64), ("dim", _c_i64), ("dstate", _c_i64),
+        ("x_row_stride", _c_i64), ("delta_row_stride", _c_i64), ("z_row_stride", _c_i64),
+        ("B_row_stride", _c_i64), ("C_row_stride", _c_i64), ("state_stride", _c_i64 * 2),
+        ("beta", _c_f), ("alpha", _c_f), ("delta_softplus", _c_i32), ("reserved", _c_i32),
+    ]
+
+
 _DESC_P = ctypes.POINTER(MMScanDesc)
 _TENS_P = ctypes.POINTER(MMScanTensors)
 _I64_P = ctypes.POINTER(_c_i64)
@@ -66,6 +76,12 @@ _SIGNATURES = {
                                             _c_p, _c_p, _c_p]),
     "mmb_mmscan_carry_bwd": (ctypes.c_int, [_c_i64, _c_i64, _I64_P, _c_i64, _c_i64, _c_i64, _c_f,
                                             _c_p, _c_p, _c_p, _c_p]),
+    "mmb_conv1d_silu_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i32, _c_p, _I64_P]
+                            + [_c_p] * 6),
+    "mmb_conv1d_silu_bwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i32, _c_p, _I64_P]
+                            + [_c_p] * 8),
+    "mmb_conv1d_step": (ctypes.c_int, [_c_i64, _c_i64, _c_i32, _c_p, _c_i64] + [_c_p] * 6),
+    "mmb_mmscan_step": (ctypes.c_int, [ctypes.POINTER(StepDesc)] + [_c_p] * 14),
     "mmb_rows_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p]),
     "mmb_rows_bwd": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p]),
     "mmb_pscan_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p]),

@@ -16,6 +16,11 @@ CUDA kernels; there is no CPU path:
       PScan-layout kernel (one scan when |beta| < 1e-6).
   "sequential"
       the row-scan kernel of momentum_scan_cuda on the materialised tensors.
+
+In every mode the block's causal depthwise conv1d + SiLU is one kernel
+(conv.conv1d_silu, no transposes), and ``step()`` runs the conv-cache update
+and the state update (with the dt softplus and the SiLU(z) gate) as one kernel
+each (conv.conv1d_step, conv.mmscan_step).
 """
 from __future__ import annotations
 
@@ -27,6 +32,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from .conv import conv1d_silu, conv1d_step, mmscan_step
 from .momentum_scan_cuda import momentum_scan_cuda
 from .pscan import pscan
 from .selective_scan import selective_scan_momentum_fn
@@ -172,9 +178,8 @@ class MambaMomentumBlock(nn.Module):
 
     # ------------------------------------------------------------------ #
     def _conv_silu(self, x):
-        L = x.shape[1]
-        x = self.conv1d(x.transpose(1, 2))[:, :, :L].transpose(1, 2)
-        return F.silu(x)
+        """silu(causal depthwise conv1d(x)) in one kernel (mamba_momentum.py:217-223)."""
+        return conv1d_silu(x, self.conv1d.weight, self.conv1d.bias)
 
     def forward(self, x):
         xz = self.in_proj(x)
@@ -248,33 +253,24 @@ class MambaMomentumBlock(nn.Module):
 
     # -------------------------- inference -------------------------- #
     def step(self, x, cache):
-        """One token (mamba_momentum.py:439-471); cache = (h, v, conv inputs)."""
+        """One token (mamba_momentum.py:439-471); cache = (h, v, conv inputs).
+        The conv-cache update and the state update with the dt softplus and the
+        SiLU(z) gate are one kernel each; the returned cache is new tensors, as
+        in the reference."""
         h, v, inputs = cache
         xz = self.in_proj(x)
         x, z = xz.chunk(2, dim=1)
-        x_cache = x.unsqueeze(2)
-        x = self.conv1d(torch.cat([inputs, x_cache], dim=2))[:, :, self.config.d_conv - 1]
-        x = F.silu(x)
-        y, h, v = self.ssm_momentum_step(x, h, v)
-        out = self.out_proj(y * F.silu(z))
-        inputs = torch.cat([inputs[:, :, 1:], x_cache], dim=2)
-        return out, (h, v, inputs)
+        x, inputs = conv1d_step(x, inputs, self.conv1d.weight, self.conv1d.bias)
+        y, h, v = self._ssm_step(x, h, v, z)
+        return self.out_proj(y), (h, v, inputs)
+
+    def _ssm_step(self, x, h, v, z):
+        A, delta, B, C = self._project(x)
+        delta_raw = F.linear(delta, self.dt_proj.weight)  # bias and softplus in-kernel
+        return mmscan_step(x, delta_raw, A, B, C, h, v, D=self.D.float(), z=z,
+                           delta_bias=self.dt_proj.bias.float(), delta_softplus=True,
+                           beta=self.momentum_beta, alpha=self.momentum_alpha)
 
     def ssm_momentum_step(self, x, h, v):
-        """Single-step state update (mamba_momentum.py:473-515)."""
-        A = -torch.exp(self.A_log.float())
-        dbc = self.x_proj(x)
-        r, n = self.config.dt_rank, self.config.d_state
-        delta, B, C = torch.split(dbc, [r, n, n], dim=-1)
-        delta, B, C = self._apply_layernorms(delta, B, C)
-        delta = F.softplus(self.dt_proj(delta))
-        deltaA = torch.exp(delta.unsqueeze(-1) * A)
-        u = self.momentum_alpha * (delta.unsqueeze(-1) * B.unsqueeze(1)) * x.unsqueeze(-1)
-        if h is None:
-            h = torch.zeros(x.size(0), self.config.d_inner, n, device=x.device)
-        if v is None:
-            v = torch.zeros(x.size(0), self.config.d_inner, n, device=x.device)
-        v = self.momentum_beta * v + u
-        h = deltaA * h + v
-        y = (h @ C.unsqueeze(-1)).squeeze(2) + self.D.float() * x
-        return y, h, v
+        """Single-step state update (mamba_momentum.py:473-515): (y, h, v)."""
+        return self._ssm_step(x, h, v, None)

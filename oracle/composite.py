@@ -204,3 +204,52 @@ def to64(*ts):
         t = t.to(torch.complex128) if t.is_complex() else t.to(_F64)
         out.append(t.detach().clone().requires_grad_(True))
     return out
+
+
+# ---------------------------------------------------------------------------
+# the momentum block's producer and decode step, fp64 torch restatements
+# ---------------------------------------------------------------------------
+def conv1d_silu(x, weight, bias=None, state_in=None):
+    """silu(causal depthwise conv1d over time) of x (B, L, D)
+    (mamba_momentum.py:217-223: conv1d with groups = D, padding = W-1, first L
+    outputs); state_in (B, D, W-1) are the inputs before t = 0."""
+    Bsz, L, D = x.shape
+    W = weight.shape[-1]
+    xt = x.transpose(1, 2)
+    if state_in is not None:
+        y = F.conv1d(torch.cat([state_in, xt], 2), weight.reshape(D, 1, W), bias, groups=D)
+    else:
+        y = F.conv1d(xt, weight.reshape(D, 1, W), bias, padding=W - 1, groups=D)[:, :, :L]
+    return F.silu(y.transpose(1, 2))
+
+
+def conv1d_step(x, conv_state, weight, bias=None, out_state=None):
+    """One token (mamba_momentum.py:455-459, :466): (silu(conv over
+    [conv_state | x]), the shifted state)."""
+    D, W = x.shape[1], weight.shape[-1]
+    cat = torch.cat([conv_state, x.unsqueeze(2)], 2)
+    y = F.conv1d(cat, weight.reshape(D, 1, W), bias, padding=W - 1, groups=D)[:, :, W - 1]
+    return F.silu(y), cat[:, :, 1:]
+
+
+def mmscan_step(x, delta, A, B, C, h=None, v=None, D=None, z=None, delta_bias=None,
+                delta_softplus=False, beta=0.6, alpha=1.0, h_out=None, v_out=None):
+    """One token of the momentum scan (mamba_momentum.py:473-515) and the block's
+    gate (:461-464): (y, h, v)."""
+    dt = delta if delta_bias is None else delta + delta_bias
+    if delta_softplus:
+        dt = F.softplus(dt)
+    a = torch.exp(dt.unsqueeze(-1) * A)
+    u = alpha * (dt.unsqueeze(-1) * B.unsqueeze(1)) * x.unsqueeze(-1)
+    if h is None:
+        h = torch.zeros_like(u)
+    if v is None:
+        v = torch.zeros_like(u)
+    v = beta * v + u
+    h = a * h + v
+    y = (h * C.unsqueeze(1)).sum(-1)
+    if D is not None:
+        y = y + D * x
+    if z is not None:
+        y = y * F.silu(z)
+    return y, h, v

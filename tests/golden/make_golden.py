@@ -27,6 +27,13 @@ complex tensors).  What each fixture exercises:
                LinOSS_pytorch.LinOSSLayer forward on a (B, L, H) batch (vmap path)
   mlin_im / mlin_imex
                mamba_linoss.apply_linoss_vectorized(..., scan_algorithm='vectorized')
+  mm_block     MambaMomentumBlock.forward (mamba_momentum.py:209-232: in_proj,
+               causal depthwise conv1d + SiLU, x_proj, dt_proj + softplus, the
+               momentum scan, SiLU(z) gate, out_proj) with its parameters,
+               input, output, and the gradients of the input and every
+               parameter for a random upstream gradient
+  mm_step      the same block's step() (mamba_momentum.py:439-515) over 6
+               tokens from an empty cache: the outputs and the final cache
   mm_state_dict.json
                parameter names and shapes of the reference MambaMomentum
                (d_model=128, n_layers=2, dt_rank=8): the module tree a drop-in
@@ -99,6 +106,52 @@ def gen_mm_seq(ref, seed):
     gh = torch.randn(h.shape, generator=g)
     ga, gu = torch.autograd.grad(h, [a_, u_], gh)
     _save("mm_seq", deltaA=dA, u=u, beta=beta, h=h, gh=gh, ddeltaA=ga, du=gu)
+
+
+def _mm_block(ref, seed):
+    mm = ref["mamba_momentum"]
+    torch.manual_seed(seed)
+    cfg = mm.MambaMomentumConfig(d_model=16, n_layers=1, d_state=16, expand_factor=2,
+                                 d_conv=4, dt_rank=4, momentum_beta=0.8, momentum_alpha=0.9,
+                                 bias=True, conv_bias=True)
+    blk = mm.MambaMomentumBlock(cfg)
+    with torch.no_grad():   # move A_log, D, conv bias off their constant inits
+        blk.A_log.add_(0.1 * torch.randn(blk.A_log.shape))
+        blk.D.add_(0.2 * torch.randn(blk.D.shape))
+        blk.conv1d.bias.add_(0.1 * torch.randn(blk.conv1d.bias.shape))
+    params = {k: v.detach().clone() for k, v in blk.state_dict().items()}
+    return blk, params
+
+
+def gen_mm_block(ref, seed):
+    blk, params = _mm_block(ref, seed)
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, 37, 16, generator=g)
+    xi = x.clone().requires_grad_(True)
+    y = blk(xi)
+    gy = torch.randn(y.shape, generator=g)
+    names = [k for k, _ in blk.named_parameters()]
+    grads = torch.autograd.grad(y, [xi] + [p for _, p in blk.named_parameters()], gy)
+    _save("mm_block", x=x, y=y, gy=gy, dx=grads[0],
+          **{"p." + k: v for k, v in params.items()},
+          **{"g." + k: gr for k, gr in zip(names, grads[1:])})
+
+
+def gen_mm_step(ref, seed):
+    blk, params = _mm_block(ref, seed)
+    g = torch.Generator().manual_seed(seed + 100)
+    Bsz, T = 3, 6
+    ed, n, w = blk.config.d_inner, blk.config.d_state, blk.config.d_conv
+    xs = torch.randn(T, Bsz, 16, generator=g)
+    cache = (None, None, torch.zeros(Bsz, ed, w - 1))
+    ys = []
+    with torch.no_grad():
+        for t in range(T):
+            y, cache = blk.step(xs[t], cache)
+            ys.append(y)
+    h, v, inputs = cache
+    _save("mm_step", xs=xs, ys=torch.stack(ys), h=h, v=v, inputs=inputs,
+          **{"p." + k: val for k, val in params.items()})
 
 
 def gen_pscan(ref, name, L, seed):
@@ -247,6 +300,8 @@ def main():
     gen_lin_layer(ref, "IMEX", seed=11)
     gen_mlin(ref, "IM", seed=12)
     gen_mlin(ref, "IMEX", seed=13)
+    gen_mm_block(ref, seed=14)
+    gen_mm_step(ref, seed=14)
     gen_state_dict(ref)
 
 

@@ -291,6 +291,7 @@ def test_mamba_momentum_stack_matches_oracle(monkeypatch):
         return oc.mmscan(x, delta, A, B, C, D, z, delta_bias, delta_softplus, beta, alpha)
 
     monkeypatch.setattr(mm, "selective_scan_momentum_fn", oracle_scan)
+    monkeypatch.setattr(mm, "conv1d_silu", oc.conv1d_silu)
     out_c = cpu(x.double())
     loss_c = out_c.pow(2).mean()
     loss_c.backward()
