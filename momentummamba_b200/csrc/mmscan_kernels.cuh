@@ -28,7 +28,8 @@
 //   gh_t = dy_t C_t + a_{t+1} gh_{t+1} ;  gv_t = gh_t + beta gv_{t+1}
 // The n-sums (dx, ddelta, recomputed y) are reduce-scattered back to the
 // owning lanes; the d-sums of the dB | dC contributions go through a per-warp
-// shared window buffer and vector reductions to global memory; dA, dD and
+// shared window buffer, then (N <= 32) a per-chunk buffer summed over the
+// CTA's warps, and vector reductions to global memory; dA, dD and
 // d(delta_bias) accumulate in registers over the sequence.
 //
 // Segments.  Over a segment of T steps the forward state maps affinely,
@@ -152,13 +153,8 @@ struct MMParams {
     float *dA, *dB, *dC, *dD, *ddbias;
 };
 
-// checkpoint record of (b, window k, channel d): 2N floats, lane ng's
-// [h(NP) | v(NP)] at ng * 2 * NP
-__device__ __forceinline__ int64_t ckpt_base(const MMParams& p, int64_t b, int64_t k, int64_t d,
-                                             int N) {
-    const int64_t K = (p.L + MM_CK - 1) / MM_CK;
-    return ((b * K + k) * p.D + d) * (int64_t)(2 * N);
-}
+// Checkpoints: record (b, window k, channel d) of 2N floats at
+// ((b K + k) D + d) 2N, K = ceil(L / 8); lane ng's [h(NP) | v(NP)] at ng * 2 * NP.
 
 template <int NP>
 __device__ __forceinline__ void ckpt_store(float* dst, const float2 (&h)[NP / 2],
@@ -290,6 +286,10 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
         ld_pairs_g<NP>(s + N, v);
     }
     float bpow = 1.f;  // SUMM: beta^(steps so far)
+    // checkpoint of block 0 of this thread; the next block's is ck_stride further
+    const int64_t ck_stride = p.D * (2 * N);
+    float* ckw = p.ckpt ? p.ckpt + (b * ((p.L + MM_CK - 1) / MM_CK) * p.D + d) * (2 * N) + ng * 2 * NP
+                        : nullptr;
     const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
     const float Dv = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
     const float alpha = p.alpha;
@@ -380,9 +380,9 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
             float nxi[IPL], ndti[IPL], ndtxi[IPL];
             if (k + 1 < NBLK) prep(sx, sdl, k + 1, nxi, ndti, ndtxi);
             // checkpoint: state before the block's first step
-            if (!SUMM && p.ckpt && dvalid) {
-                const int64_t kk = tb / MM_CK;
-                ckpt_store<NP>(p.ckpt + ckpt_base(p, b, kk, d, N) + ng * 2 * NP, h, v);
+            if (!SUMM && ckw) {
+                if (dvalid) ckpt_store<NP>(ckw, h, v);
+                ckw += ck_stride;
             }
             float y[MM_CK];
 #pragma unroll
@@ -476,6 +476,11 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
     }
 }
 
+// The backward sums dB | dC over the CTA's warps per chunk before the global
+// reductions (4x fewer atomics) when the chunk buffer fits: N <= 32.
+template <int N>
+__host__ __device__ constexpr bool mm_bwd_cbuf() { return N <= 32; }
+
 // ---------------------------------------------------------------------------
 // backward
 //
@@ -501,6 +506,10 @@ __global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) 
     // tiles: x | delta | z | dout (T x RP), B | C (T x N); then the window buffer
     MMStager<N, NP, 4, E> stg{reinterpret_cast<float*>(smem4), (int)threadIdx.x, 0, p.vec};
     float* wbuf = reinterpret_cast<float*>(smem4) + Sm::FLOATS;
+    // chunk buffer (N <= 32): each warp's d-sums of dB | dC for the 32 steps of
+    // a chunk, [warp][step][2N]; summed over the CTA's warps once per chunk
+    constexpr bool CBUF = mm_bwd_cbuf<N>();
+    float4* cbuf = reinterpret_cast<float4*>(wbuf + MM_CK * DT * 2 * N);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ng = lane & (G - 1);
@@ -551,8 +560,14 @@ __global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) 
     float2 nck_h[NP2], nck_v[NP2];  // checkpoint of the next window to process
 #pragma unroll
     for (int j = 0; j < NP2; ++j) nck_h[j] = nck_v[j] = f2(0.f);
-    auto ck_load = [&](int64_t k) {
-        if (dvalid) ckpt_load<NP>(p.ckpt_in + ckpt_base(p, b, k, d, N) + ng * 2 * NP, nck_h, nck_v);
+    // windows are visited in decreasing order: a running pointer to the next
+    // checkpoint (starting at the last one), one stride back per load
+    const int64_t ck_stride = p.D * (2 * N);
+    const int64_t nck = (p.L + MM_CK - 1) / MM_CK;
+    const float* ckp = p.ckpt_in + ((b * nck + nck - 1) * p.D + d) * (2 * N) + ng * 2 * NP;
+    auto ck_next = [&]() {
+        if (dvalid) ckpt_load<NP>(ckp, nck_h, nck_v);
+        ckp -= ck_stride;
     };
 
     auto stage = [&](int slot, int c) {
@@ -592,14 +607,14 @@ __global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) 
         for (int w = (Lc - 1) / MM_CK; w >= 0; --w) {
             const int w0 = w * MM_CK;
             // window checkpoint (loaded one window ahead)
-            if (it == 0 && w == (Lc - 1) / MM_CK) ck_load((t0 + w0) / MM_CK);
+            if (it == 0 && w == (Lc - 1) / MM_CK) ck_next();
             float2 h[NP2], v[NP2];
 #pragma unroll
             for (int j = 0; j < NP2; ++j) {
                 h[j] = nck_h[j];
                 v[j] = nck_v[j];
             }
-            if (t0 + w0 > 0) ck_load((t0 + w0) / MM_CK - 1);
+            if (t0 + w0 > 0) ck_next();
             // this lane's items: dt, alpha*dt*x, dy = dout*silu(z)
             float xi[IPL], ri[IPL], dti[IPL], dtxi[IPL], dyi[IPL];
 #pragma unroll
@@ -750,17 +765,44 @@ __global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) 
                         acc23.x += __shfl_xor_sync(FULL, acc23.x, m);
                         acc23.y += __shfl_xor_sync(FULL, acc23.y, m);
                     }
-                    const int64_t gt = t0 + w0 + s;
-                    if (part == 0 && gt < p.L) {
-                        const int col = q * 4;
-                        float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
-                        red_add_v4(dst, acc01.x, acc01.y, acc23.x, acc23.y);
+                    if constexpr (CBUF) {
+                        if (part == 0)
+                            cbuf[(warp * T + w0 + s) * NQ + q] =
+                                make_float4(acc01.x, acc01.y, acc23.x, acc23.y);
+                    } else {
+                        const int64_t gt = t0 + w0 + s;
+                        if (part == 0 && gt < p.L) {
+                            const int col = q * 4;
+                            float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
+                            red_add_v4(dst, acc01.x, acc01.y, acc23.x, acc23.y);
+                        }
                     }
                 }
             }
             __syncwarp();
         }
         __syncthreads();
+        if constexpr (CBUF) {
+            // the chunk's dB | dC: sum over the CTA's warps, one vector reduction
+            // to global memory per (step, 4 columns)
+            constexpr int ITEMS = T * NQ;
+#pragma unroll
+            for (int i = tid; i < ITEMS; i += MM_NT) {
+                const int s = i / NQ, q = i % NQ;
+                float2 a01 = f2(0.f), a23 = f2(0.f);
+#pragma unroll
+                for (int wi = 0; wi < MM_NT / 32; ++wi) {
+                    const float4 vv = cbuf[(wi * T + s) * NQ + q];
+                    a01 = fadd2(a01, make_float2(vv.x, vv.y));
+                    a23 = fadd2(a23, make_float2(vv.z, vv.w));
+                }
+                if (s < Lc) {
+                    const int col = q * 4;
+                    float* dst = (col < N ? p.dB : p.dC) + (b * p.L + t0 + s) * N + (col % N);
+                    red_add_v4(dst, a01.x, a01.y, a23.x, a23.y);
+                }
+            }
+        }
     }
 
     if (p.gstate_out && dvalid) {
@@ -939,7 +981,8 @@ template <int N, int NP, bool SP, bool Z, class E>
 int launch_bwd_t(const MMParams& p, cudaStream_t stream) {
     using Cf = MMCfg<N, NP>;
     const size_t smem =
-        sizeof(float) * (MMSmem<N, NP, 4, E::BYTES>::FLOATS + MM_CK * Cf::DT * 2 * N);
+        sizeof(float) * (MMSmem<N, NP, 4, E::BYTES>::FLOATS + MM_CK * Cf::DT * 2 * N +
+                         (mm_bwd_cbuf<N>() ? (MM_NT / 32) * MM_T * 2 * N : 0));
     static int attr_done[MMB_MAX_DEVICES] = {};
     const int st = mmb_smem_attr(mmscan_bwd_kernel<N, NP, SP, Z, E>, smem, attr_done);
     if (st != MMB_OK) return st;
