@@ -47,6 +47,12 @@ int mmb_abi_version(void);
  * thread (static storage), or "no CUDA error recorded". */
 const char* mmb_last_error(void);
 
+/* Synchronises `stream`, then reports whether a kernel of this library on the
+ * current device gave up a bounded device-side wait since the last call
+ * (MMB_ERR_TIMEOUT; the flag is cleared) -- the shared-memory tile pipelines
+ * wait on transaction barriers with an iteration limit.  MMB_OK otherwise. */
+int mmb_device_status(mmb_stream_t stream);
+
 /* =========================================================================
  * Momentum selective scan (fused discretisation, scan, C-contraction, D skip,
  * optional softplus(delta + bias) and optional SiLU(z) gate):

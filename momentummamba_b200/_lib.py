@@ -65,6 +65,7 @@ _SIGNATURES = {
     "mmb_status_string": (ctypes.c_char_p, [ctypes.c_int]),
     "mmb_abi_version": (ctypes.c_int, []),
     "mmb_last_error": (ctypes.c_char_p, []),
+    "mmb_device_status": (ctypes.c_int, [_c_p]),
     "mmb_mmscan_ckpt_floats": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "mmb_mmscan_fwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 10 + [_c_p]),
     "mmb_mmscan_bwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 18 + [_c_p]),

@@ -1,6 +1,7 @@
 // Shared device helpers for the sm_100a scan kernels.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -127,6 +128,57 @@ struct ElemBF16 {
     __device__ static float load(const T* p, int64_t i) { return bf16_lo(p[i]); }
     __device__ static void store(T* p, int64_t i, float v) { p[i] = f32_to_bf16(v); }
 };
+
+// ---------------------------------------------------------------------------
+// TMA tile loads and mbarriers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+// make the barrier inits visible to the async (TMA) proxy
+__device__ __forceinline__ void mbar_fence_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;\n\tfence.proxy.async.shared::cta;" ::
+                     : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Wait for phase `parity` of the barrier, giving up after a bounded number of
+// polls (each poll itself suspends for a hardware-chosen while): false then.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    for (int i = 0; i < (1 << 22); ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    return false;
+}
+
+// 3-D tiled TMA load of the box at (c0, c1, c2) into shared memory, completing
+// on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_3d(void* sdst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(sdst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
 
 // ---------------------------------------------------------------------------
 // math
@@ -277,6 +329,17 @@ __device__ __forceinline__ void red_add_v4(float* gaddr, float a, float b, float
 
 // Last CUDA error seen by this library on the calling thread (see mmb_last_error).
 void mmb_record_cuda_error(cudaError_t e);
+
+// Device address of the error flag that bounded device waits set (current device).
+int* mmb_device_error_flag();
+
+// Encode a 3-D tiled tensor map over dims (dim0 innermost, unit stride; dim1 and
+// dim2 with element strides stride1, stride2) for boxes of box0 x box1 x 1
+// elements of elem_bytes (4: fp32, 2: bf16), swizzle span 0/32/64/128 bytes,
+// out-of-range elements read as zero.  false if the driver refuses.
+bool mmb_encode_tile_map(CUtensorMap* map, const void* base, int elem_bytes, int64_t dim0,
+                         int64_t dim1, int64_t dim2, int64_t stride1, int64_t stride2,
+                         int box0, int box1, int swizzle_bytes);
 
 // Host-side launch-status helper shared by the C-ABI wrappers.
 static inline int mmb_launch_status() {

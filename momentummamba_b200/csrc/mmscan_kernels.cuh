@@ -67,17 +67,27 @@ struct MMCfg {
     static constexpr int DT = MM_NT / G;              // channels per CTA
     static constexpr int DPW = 32 / G;                // channels per warp
     static constexpr int LOG2DPW = 5 - LOG2G;
-    // (T x DT) fp32 tile pitch: the rows and channels a warp reads at once fall
-    // in distinct banks
-    static constexpr int RP = G >= 16 ? DT + 4 : DT + DPW;
-    static constexpr int TR = MM_T * RP;
+    // (T x DT) fp32 activation tile: dense rows of DT floats whose 16-byte
+    // chunks are XOR-swizzled across rows -- the TMA swizzle of a DT*4-byte row
+    // (up to 128 bytes) -- so the rows and channels a warp reads at once fall
+    // in distinct banks.  (T x N) tiles of B and C are dense, unswizzled.
+    static constexpr int TR = MM_T * DT;
+    static constexpr int SWB = DT * 4 <= 128 ? DT * 4 : 0;  // swizzle span in bytes
+    static constexpr int SWM = SWB ? SWB / 4 - 4 : 0;        // its XOR mask in floats
+    __host__ __device__ static constexpr int dix(int r, int c) {
+        return (r * DT + c) ^ (((r * DT + c) >> 3) & SWM);
+    }
     static constexpr int TN = MM_T * N;
     static_assert((NP == 2 || NP == 4) && N % NP == 0 && G >= 2 && G <= 16, "unsupported shape");
 };
 
 // Shared-memory layout of one kernel: NDT (T x DT) activation tiles and two
-// (T x N) tiles per chunk.  fp32 activations: MM_NS fp32 stages.  bf16: one
-// fp32 working stage plus MM_NS raw 16-bit stages that cp.async fills.
+// (T x N) tiles per chunk.  fp32 activations: MM_NS fp32 stages, filled by TMA
+// (or cp.async when the rows are not 16-byte aligned).  bf16: one fp32 working
+// stage plus MM_NS raw 16-bit stages that TMA (or cp.async) fills and the
+// kernel widens.  Stages start on 1024-byte boundaries (the swizzle period);
+// MM_SMEM_ALIGN bytes of slack let the kernel align its dynamic base.
+constexpr int MM_SMEM_ALIGN = 1024;
 template <int N, int NP, int NDT, int EBYTES>
 struct MMSmem {
     using Cf = MMCfg<N, NP>;
@@ -85,7 +95,64 @@ struct MMSmem {
     static constexpr int F32 = NDT * Cf::TR + 2 * Cf::TN;             // floats per fp32 stage
     static constexpr int RAW = NDT * MM_T * Cf::DT + 2 * MM_T * N;    // 16-bit words per raw stage
     static constexpr int FLOATS = WIDE ? F32 + MM_NS * RAW / 2 : MM_NS * F32;
+    static_assert((F32 * 4) % MM_SMEM_ALIGN == 0, "stage size keeps the swizzle period");
 };
+
+// The kernel's dynamic shared memory, aligned up to the swizzle period.
+__device__ __forceinline__ float* mm_smem_base(float4* raw) {
+    const uint32_t s = smem_u32(raw);
+    return reinterpret_cast<float*>(reinterpret_cast<char*>(raw) +
+                                    ((MM_SMEM_ALIGN - (s & (MM_SMEM_ALIGN - 1))) &
+                                     (MM_SMEM_ALIGN - 1)));
+}
+
+// TMA descriptors of one launch: x, delta, z, dout tiles (T x DT, swizzled for
+// fp32) and B, C tiles (T x N).
+struct MMTmaps {
+    CUtensorMap m[6];
+};
+enum { TM_X = 0, TM_DELTA = 1, TM_Z = 2, TM_DOUT = 3, TM_B = 4, TM_C = 5 };
+
+// fp32 (ROWS x COLS) tile into a dense shared tile with the XOR swizzle SWM:
+// 16-byte copies when `vec` (rows 16-byte aligned, cvalid % 4 == 0), else 4-byte.
+template <int ROWS, int COLS, int SWM, int NTHREADS>
+__device__ __forceinline__ void stage_tile_swz(float* s, const float* g, int64_t gstride,
+                                               int rvalid, int cvalid, bool vec, int tid) {
+    if (vec) {
+        constexpr int C4 = COLS / 4;
+#pragma unroll
+        for (int i = tid; i < ROWS * C4; i += NTHREADS) {
+            const int r = i / C4, c = (i % C4) * 4;
+            const bool ok = (r < rvalid) && (c < cvalid);
+            const int e = r * COLS + c;
+            cp_async16(s + (e ^ ((e >> 3) & SWM)), ok ? g + (int64_t)r * gstride + c : g, ok);
+        }
+    } else {
+#pragma unroll 4
+        for (int i = tid; i < ROWS * COLS; i += NTHREADS) {
+            const int r = i / COLS, c = i % COLS;
+            const bool ok = (r < rvalid) && (c < cvalid);
+            const int e = r * COLS + c;
+            cp_async4(s + (e ^ ((e >> 3) & SWM)), ok ? g + (int64_t)r * gstride + c : g, ok);
+        }
+    }
+}
+
+// Widen a dense (ROWS x COLS) bf16 tile into an fp32 tile with the swizzle SWM.
+template <int ROWS, int COLS, int SWM, int NTHREADS>
+__device__ __forceinline__ void widen_tile_swz(float* dst, const uint16_t* src, int tid) {
+    constexpr int C8 = COLS / 8;
+#pragma unroll
+    for (int i = tid; i < ROWS * C8; i += NTHREADS) {
+        const int r = i / C8, c = (i % C8) * 8;
+        const uint4 q = *reinterpret_cast<const uint4*>(src + r * COLS + c);
+        const int e0 = r * COLS + c, e1 = e0 + 4;
+        *reinterpret_cast<float4*>(dst + (e0 ^ ((e0 >> 3) & SWM))) =
+            make_float4(bf16_lo(q.x), bf16_hi(q.x), bf16_lo(q.y), bf16_hi(q.y));
+        *reinterpret_cast<float4*>(dst + (e1 ^ ((e1 >> 3) & SWM))) =
+            make_float4(bf16_lo(q.z), bf16_hi(q.z), bf16_lo(q.w), bf16_hi(q.w));
+    }
+}
 
 // Lane (within its channel's group) that owns step s of an 8-step block: the
 // inverse of the reduce-scatter placement rs_index<8, LB>.
@@ -139,6 +206,8 @@ struct MMParams {
     float beta, alpha;
     int softplus;
     int vec;  // 16-byte staging allowed
+    int tma;  // tiles come by TMA (the launch's tensor maps are valid)
+    int* err; // set when a bounded wait gives up
     const float* state_in;  // (Bsz, D, 2, N): h | v before the first step, or null
     float* state_out;       // (Bsz, D, 2, N) after the last step, or null
     const float* ckpt_in;
@@ -183,37 +252,75 @@ __device__ __forceinline__ void ckpt_load(const float* src, float2 (&h)[NP / 2],
 }
 
 // Chunk staging shared by the kernels: D-tile i of a chunk holds (T x DT)
-// activations, N-tile j (T x N) of B or C.  `slot` is the pipeline stage.
+// activations, N-tile j (T x N) of B or C; `slot` is the pipeline stage.  With
+// TMA (p.tma) thread 0 arms the stage's transaction barrier with the bytes of
+// the tiles it is about to copy and issues one tensor copy per tile; the other
+// threads only wait on the barrier.  Otherwise every thread issues cp.async
+// copies and waits on its own groups.
 template <int N, int NP, int NDT, class E>
 struct MMStager {
     using Cf = MMCfg<N, NP>;
     using Sm = MMSmem<N, NP, NDT, E::BYTES>;
     using ET = typename E::T;
-    float* smem;
-    int tid, dcols, vec;
+    float* smem;      // aligned dynamic base
+    uint64_t* bars;   // MM_NS transaction barriers
+    const MMTmaps* tm;
+    int tid, dcols, vec, tma;
 
     __device__ uint16_t* raw(int slot) const {
         return reinterpret_cast<uint16_t*>(smem + Sm::F32) + slot * Sm::RAW;
     }
-    __device__ void tile_d(int slot, int i, const ET* g, int64_t gstride, int rows) const {
+    __device__ void* dtile(int slot, int i) const {
+        if constexpr (Sm::WIDE) return raw(slot) + i * MM_T * Cf::DT;
+        else return smem + slot * Sm::F32 + i * Cf::TR;
+    }
+    __device__ void* ntile(int slot, int j) const {
+        if constexpr (Sm::WIDE) return raw(slot) + NDT * MM_T * Cf::DT + j * MM_T * N;
+        else return smem + slot * Sm::F32 + NDT * Cf::TR + j * Cf::TN;
+    }
+    // open a stage that will hold nd activation tiles and nn B/C tiles
+    __device__ void begin(int slot, int nd, int nn) const {
+        if (tma && tid == 0)
+            mbar_expect_tx(&bars[slot], (uint32_t)((nd * Cf::TR + nn * Cf::TN) * E::BYTES));
+    }
+    __device__ void tile_d(int slot, int i, int map, int64_t d0, int64_t t0, int64_t b,
+                           const ET* g, int64_t gstride, int rows) const {
+        if (tma) {
+            if (tid == 0) tma_load_3d(dtile(slot, i), &tm->m[map], (int)d0, (int)t0, (int)b, &bars[slot]);
+            return;
+        }
         if constexpr (Sm::WIDE)
-            stage_tile_b16<MM_T, Cf::DT, Cf::DT, MM_NT>(raw(slot) + i * MM_T * Cf::DT,
+            stage_tile_b16<MM_T, Cf::DT, Cf::DT, MM_NT>(static_cast<uint16_t*>(dtile(slot, i)),
                                                         reinterpret_cast<const uint16_t*>(g),
                                                         gstride, rows, dcols, tid);
         else
-            stage_tile<MM_T, Cf::DT, Cf::RP, MM_NT>(smem + slot * Sm::F32 + i * Cf::TR,
-                                                    reinterpret_cast<const float*>(g), gstride,
-                                                    rows, dcols, vec, tid);
+            stage_tile_swz<MM_T, Cf::DT, Cf::SWM, MM_NT>(static_cast<float*>(dtile(slot, i)),
+                                                         reinterpret_cast<const float*>(g),
+                                                         gstride, rows, dcols, vec, tid);
     }
-    __device__ void tile_n(int slot, int j, const ET* g, int64_t gstride, int rows) const {
+    __device__ void tile_n(int slot, int j, int map, int64_t t0, int64_t b, const ET* g,
+                           int64_t gstride, int rows) const {
+        if (tma) {
+            if (tid == 0) tma_load_3d(ntile(slot, j), &tm->m[map], 0, (int)t0, (int)b, &bars[slot]);
+            return;
+        }
         if constexpr (Sm::WIDE)
-            stage_tile_b16<MM_T, N, N, MM_NT>(raw(slot) + NDT * MM_T * Cf::DT + j * MM_T * N,
+            stage_tile_b16<MM_T, N, N, MM_NT>(static_cast<uint16_t*>(ntile(slot, j)),
                                               reinterpret_cast<const uint16_t*>(g), gstride, rows,
                                               N, tid);
         else
-            stage_tile<MM_T, N, N, MM_NT>(smem + slot * Sm::F32 + NDT * Cf::TR + j * Cf::TN,
-                                          reinterpret_cast<const float*>(g), gstride, rows, N,
-                                          vec, tid);
+            stage_tile_swz<MM_T, N, 0, MM_NT>(static_cast<float*>(ntile(slot, j)),
+                                              reinterpret_cast<const float*>(g), gstride, rows,
+                                              N, vec, tid);
+    }
+    __device__ void commit() const {
+        if (!tma) cp_async_commit();
+    }
+    // wait until the use-th fill of `slot` landed; false when a bounded wait gave up
+    __device__ bool wait(int slot, int use) const {
+        if (tma) return mbar_wait_bounded(&bars[slot], (uint32_t)(use & 1));
+        cp_async_wait<MM_NS - 1>();
+        return true;
     }
     // After the stage's copies landed (and a barrier): the fp32 view of it.
     // bf16 widens the tiles named by the masks into the working stage; the
@@ -224,13 +331,13 @@ struct MMStager {
 #pragma unroll
             for (int i = 0; i < NDT; ++i)
                 if (dmask & (1u << i))
-                    widen_tile<MM_T, Cf::DT, Cf::DT, Cf::RP, MM_NT>(smem + i * Cf::TR,
-                                                                    r + i * MM_T * Cf::DT, tid);
+                    widen_tile_swz<MM_T, Cf::DT, Cf::SWM, MM_NT>(smem + i * Cf::TR,
+                                                                 r + i * MM_T * Cf::DT, tid);
 #pragma unroll
             for (int j = 0; j < 2; ++j)
                 if (nmask & (1u << j))
-                    widen_tile<MM_T, N, N, N, MM_NT>(smem + NDT * Cf::TR + j * Cf::TN,
-                                                     r + NDT * MM_T * Cf::DT + j * MM_T * N, tid);
+                    widen_tile_swz<MM_T, N, 0, MM_NT>(smem + NDT * Cf::TR + j * Cf::TN,
+                                                      r + NDT * MM_T * Cf::DT + j * MM_T * N, tid);
             return smem;
         } else {
             return smem + slot * Sm::F32;
@@ -238,19 +345,32 @@ struct MMStager {
     }
 };
 
+// Barrier set-up of the TMA pipeline (all threads call; one thread inits).
+__device__ __forceinline__ void mm_pipe_init(uint64_t* bars, bool tma) {
+    if (tma && threadIdx.x == 0) {
+#pragma unroll
+        for (int s = 0; s < MM_NS; ++s) mbar_init(&bars[s], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+}
+
 // ---------------------------------------------------------------------------
 // forward (SUMM: the segment summary instead -- no C, z, y or checkpoints)
 // ---------------------------------------------------------------------------
 template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, bool SUMM>
-__global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
+__global__ void __launch_bounds__(MM_NT)
+    mmscan_fwd_kernel(const MMParams p, const __grid_constant__ MMTmaps tmaps) {
     using Cf = MMCfg<N, NP>;
     using ET = typename E::T;
-    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, RP = Cf::RP, IPL = Cf::IPL, LB = Cf::LB;
+    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, IPL = Cf::IPL, LB = Cf::LB;
     constexpr int NP2 = Cf::NP2, NBLK = T / MM_CK;
     static_assert(!(SUMM && HAS_Z), "the summary has no gate");
     extern __shared__ float4 smem4[];
-    // tiles: x | delta | z (T x RP), B | C (T x N)
-    MMStager<N, NP, 3, E> stg{reinterpret_cast<float*>(smem4), (int)threadIdx.x, 0, p.vec};
+    __shared__ uint64_t bars[MM_NS];
+    // tiles: x | delta | z (T x DT), B | C (T x N)
+    MMStager<N, NP, 3, E> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0, p.vec, p.tma};
+    mm_pipe_init(bars, p.tma);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ng = lane & (G - 1);
@@ -304,18 +424,22 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
     auto stage = [&](int slot, int c) {
         const int64_t t0 = (int64_t)c * T;
         const int rv = (int)min64(T, p.L - t0);
-        stg.tile_d(slot, 0, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
-        stg.tile_d(slot, 1, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1], rv);
-        if (HAS_Z) stg.tile_d(slot, 2, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1], rv);
-        stg.tile_n(slot, 0, gB + b * p.bs[0] + t0 * p.bs[1], p.bs[1], rv);
-        if (!SUMM) stg.tile_n(slot, 1, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
+        stg.begin(slot, HAS_Z ? 3 : 2, SUMM ? 1 : 2);
+        stg.tile_d(slot, 0, TM_X, d0, t0, b, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
+        stg.tile_d(slot, 1, TM_DELTA, d0, t0, b, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1],
+                   rv);
+        if (HAS_Z)
+            stg.tile_d(slot, 2, TM_Z, d0, t0, b, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1],
+                       rv);
+        stg.tile_n(slot, 0, TM_B, t0, b, gB + b * p.bs[0] + t0 * p.bs[1], p.bs[1], rv);
+        if (!SUMM) stg.tile_n(slot, 1, TM_C, t0, b, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
     };
     // this lane's items of block k: x, dt, alpha*dt*x
     auto prep = [&](const float* sx, const float* sdl, int k, float (&xi)[IPL], float (&dti)[IPL],
                     float (&dtxi)[IPL]) {
 #pragma unroll
         for (int i = 0; i < IPL; ++i) {
-            const int row = (k * MM_CK + ibase + i) * RP + dl;
+            const int row = Cf::dix(k * MM_CK + ibase + i, dl);
             xi[i] = sx[row];
             const float r = sdl[row] + bias_d;
             dti[i] = SOFTPLUS ? softplus_f(r) : r;
@@ -328,14 +452,17 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
 #pragma unroll
     for (int c = 0; c < MM_NS - 1; ++c) {
         if (c < nchunks) stage(c, c);
-        cp_async_commit();
+        stg.commit();
     }
     const float* st = nullptr;
     for (int c = 0; c < nchunks; ++c) {
         if (c + MM_NS - 1 < nchunks) stage((c + MM_NS - 1) % MM_NS, c + MM_NS - 1);
-        cp_async_commit();
-        cp_async_wait<MM_NS - 1>();
-        __syncthreads();
+        stg.commit();
+        const bool landed = stg.wait(c % MM_NS, c / MM_NS);
+        if (__syncthreads_or(!landed)) {
+            if (tid == 0 && p.err) atomicOr(p.err, 1);
+            return;
+        }
         st = stg.view(c % MM_NS, DMASK, NMASK);
         if (MMSmem<N, NP, 3, E::BYTES>::WIDE) __syncthreads();
         const float* sx = st;
@@ -414,7 +541,7 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
                     const int64_t gt = t0 + tt;
                     float o = fmaf(Dv, xi[i], y[i]);
                     if (HAS_Z) {
-                        const float zv = sz[tt * RP + dl];
+                        const float zv = sz[Cf::dix(tt, dl)];
                         o *= zv * sigmoid_f(zv);
                     }
                     if (item_lane && dvalid && gt < p.L) E::store(gout, (b * p.L + gt) * p.D + d, o);
@@ -444,9 +571,9 @@ __global__ void __launch_bounds__(MM_NT) mmscan_fwd_kernel(const MMParams p) {
         const int64_t t0 = (int64_t)(nchunks - 1) * T;
         for (int64_t t = tail_t; t < p.L; ++t) {
             const int tt = (int)(t - t0);
-            const float r = st[Cf::TR + tt * RP + dl] + bias_d;
+            const float r = st[Cf::TR + Cf::dix(tt, dl)] + bias_d;
             const float dt = SOFTPLUS ? softplus_f(r) : r;
-            const float dtx = alpha * dt * st[tt * RP + dl];
+            const float dtx = alpha * dt * st[Cf::dix(tt, dl)];
             float2 bq[NP2];
             ld_pairs<NP>(st + 3 * Cf::TR + tt * N + ng * NP, bq);
 #pragma unroll
@@ -494,18 +621,21 @@ __host__ __device__ constexpr bool mm_bwd_cbuf() { return N <= 32; }
 // (min 1 block per SM: without it ptxas caps the registers for 3 blocks per SM
 // and spills; the 254-register build measured 7-8 % faster)
 template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E>
-__global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) {
+__global__ void __launch_bounds__(MM_NT, 1)
+    mmscan_bwd_kernel(const MMParams p, const __grid_constant__ MMTmaps tmaps) {
     using Cf = MMCfg<N, NP>;
     using Sm = MMSmem<N, NP, 4, E::BYTES>;
     using ET = typename E::T;
-    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, RP = Cf::RP, IPL = Cf::IPL, LB = Cf::LB;
+    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, IPL = Cf::IPL, LB = Cf::LB;
     constexpr int NP2 = Cf::NP2, TR = Cf::TR, DPW = Cf::DPW;
     constexpr int NQ = 2 * N / 4;  // float4 columns per window-buffer row
     constexpr int SWZ = NQ / 2;    // float4 swizzle of odd channels (= G units of NP floats)
     extern __shared__ float4 smem4[];
-    // tiles: x | delta | z | dout (T x RP), B | C (T x N); then the window buffer
-    MMStager<N, NP, 4, E> stg{reinterpret_cast<float*>(smem4), (int)threadIdx.x, 0, p.vec};
-    float* wbuf = reinterpret_cast<float*>(smem4) + Sm::FLOATS;
+    __shared__ uint64_t bars[MM_NS];
+    // tiles: x | delta | z | dout (T x DT), B | C (T x N); then the window buffer
+    MMStager<N, NP, 4, E> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0, p.vec, p.tma};
+    mm_pipe_init(bars, p.tma);
+    float* wbuf = stg.smem + Sm::FLOATS;
     // chunk buffer (N <= 32): each warp's d-sums of dB | dC for the 32 steps of
     // a chunk, [warp][step][2N]; summed over the CTA's warps once per chunk
     constexpr bool CBUF = mm_bwd_cbuf<N>();
@@ -573,26 +703,33 @@ __global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) 
     auto stage = [&](int slot, int c) {
         const int64_t t0 = (int64_t)c * T;
         const int rv = (int)min64(T, p.L - t0);
-        stg.tile_d(slot, 0, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
-        stg.tile_d(slot, 1, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1], rv);
-        if (HAS_Z) stg.tile_d(slot, 2, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1], rv);
-        stg.tile_d(slot, 3, gdo + (b * p.L + t0) * p.D + d0, p.D, rv);
-        stg.tile_n(slot, 0, gB + b * p.bs[0] + t0 * p.bs[1], p.bs[1], rv);
-        stg.tile_n(slot, 1, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
+        stg.begin(slot, HAS_Z ? 4 : 3, 2);
+        stg.tile_d(slot, 0, TM_X, d0, t0, b, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
+        stg.tile_d(slot, 1, TM_DELTA, d0, t0, b, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1],
+                   rv);
+        if (HAS_Z)
+            stg.tile_d(slot, 2, TM_Z, d0, t0, b, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1],
+                       rv);
+        stg.tile_d(slot, 3, TM_DOUT, d0, t0, b, gdo + (b * p.L + t0) * p.D + d0, p.D, rv);
+        stg.tile_n(slot, 0, TM_B, t0, b, gB + b * p.bs[0] + t0 * p.bs[1], p.bs[1], rv);
+        stg.tile_n(slot, 1, TM_C, t0, b, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
     };
     constexpr unsigned DMASK = HAS_Z ? 15u : 11u;
 
 #pragma unroll
     for (int it = 0; it < MM_NS - 1; ++it) {
         if (it < nchunks) stage(it, nchunks - 1 - it);
-        cp_async_commit();
+        stg.commit();
     }
     for (int it = 0; it < nchunks; ++it) {
         const int c = nchunks - 1 - it;
         if (it + MM_NS - 1 < nchunks) stage((it + MM_NS - 1) % MM_NS, c - (MM_NS - 1));
-        cp_async_commit();
-        cp_async_wait<MM_NS - 1>();
-        __syncthreads();
+        stg.commit();
+        const bool landed = stg.wait(it % MM_NS, it / MM_NS);
+        if (__syncthreads_or(!landed)) {
+            if (tid == 0 && p.err) atomicOr(p.err, 1);
+            return;
+        }
         const float* st = stg.view(it % MM_NS, DMASK, 3u);
         if (Sm::WIDE) __syncthreads();
         const float* sx = st;
@@ -619,7 +756,7 @@ __global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) 
             float xi[IPL], ri[IPL], dti[IPL], dtxi[IPL], dyi[IPL];
 #pragma unroll
             for (int i = 0; i < IPL; ++i) {
-                const int row = (w0 + ibase + i) * RP + dl;
+                const int row = Cf::dix(w0 + ibase + i, dl);
                 xi[i] = sx[row];
                 ri[i] = sdl[row] + bias_d;
                 dti[i] = SOFTPLUS ? softplus_f(ri[i]) : ri[i];
@@ -723,10 +860,10 @@ __global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) 
                 const float SB = sab[2 * i + 1];
                 const float xv = xi[i];
                 if (HAS_Z) {
-                    const float zv = sz[tt * RP + dl];
+                    const float zv = sz[Cf::dix(tt, dl)];
                     const float sg = sigmoid_f(zv);
                     const float yfull = fmaf(Dv, xv, yv[i]);
-                    const float gz = sdo[tt * RP + dl] * yfull * sg * (1.f + zv * (1.f - sg));
+                    const float gz = sdo[Cf::dix(tt, dl)] * yfull * sg * (1.f + zv * (1.f - sg));
                     if (ok && gdz) E::store(gdz, gi, gz);
                 }
                 float gdt = fmaf(alpha * xv, SB, SA);
@@ -839,15 +976,18 @@ __global__ void __launch_bounds__(MM_NT, 1) mmscan_bwd_kernel(const MMParams p) 
 // forward replay.
 // ---------------------------------------------------------------------------
 template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E>
-__global__ void __launch_bounds__(MM_NT) mmscan_bwd_summary_kernel(const MMParams p) {
+__global__ void __launch_bounds__(MM_NT)
+    mmscan_bwd_summary_kernel(const MMParams p, const __grid_constant__ MMTmaps tmaps) {
     using Cf = MMCfg<N, NP>;
     using Sm = MMSmem<N, NP, 4, E::BYTES>;
     using ET = typename E::T;
-    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, RP = Cf::RP, IPL = Cf::IPL, LB = Cf::LB;
+    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, IPL = Cf::IPL, LB = Cf::LB;
     constexpr int NP2 = Cf::NP2, TR = Cf::TR;
     extern __shared__ float4 smem4[];
+    __shared__ uint64_t bars[MM_NS];
     // same tile layout as the backward; x and B are not staged
-    MMStager<N, NP, 4, E> stg{reinterpret_cast<float*>(smem4), (int)threadIdx.x, 0, p.vec};
+    MMStager<N, NP, 4, E> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0, p.vec, p.tma};
+    mm_pipe_init(bars, p.tma);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ng = lane & (G - 1);
@@ -880,24 +1020,31 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_summary_kernel(const MMParam
     auto stage = [&](int slot, int c) {
         const int64_t t0 = (int64_t)c * T;
         const int rv = (int)min64(T, p.L - t0);
-        stg.tile_d(slot, 1, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1], rv);
-        if (HAS_Z) stg.tile_d(slot, 2, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1], rv);
-        stg.tile_d(slot, 3, gdo + (b * p.L + t0) * p.D + d0, p.D, rv);
-        stg.tile_n(slot, 1, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
+        stg.begin(slot, HAS_Z ? 3 : 2, 1);
+        stg.tile_d(slot, 1, TM_DELTA, d0, t0, b, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1],
+                   rv);
+        if (HAS_Z)
+            stg.tile_d(slot, 2, TM_Z, d0, t0, b, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1],
+                       rv);
+        stg.tile_d(slot, 3, TM_DOUT, d0, t0, b, gdo + (b * p.L + t0) * p.D + d0, p.D, rv);
+        stg.tile_n(slot, 1, TM_C, t0, b, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
     };
     constexpr unsigned DMASK = HAS_Z ? 14u : 10u;
 
 #pragma unroll
     for (int it = 0; it < MM_NS - 1; ++it) {
         if (it < nchunks) stage(it, nchunks - 1 - it);
-        cp_async_commit();
+        stg.commit();
     }
     for (int it = 0; it < nchunks; ++it) {
         const int c = nchunks - 1 - it;
         if (it + MM_NS - 1 < nchunks) stage((it + MM_NS - 1) % MM_NS, c - (MM_NS - 1));
-        cp_async_commit();
-        cp_async_wait<MM_NS - 1>();
-        __syncthreads();
+        stg.commit();
+        const bool landed = stg.wait(it % MM_NS, it / MM_NS);
+        if (__syncthreads_or(!landed)) {
+            if (tid == 0 && p.err) atomicOr(p.err, 1);
+            return;
+        }
         const float* st = stg.view(it % MM_NS, DMASK, 2u);
         if (Sm::WIDE) __syncthreads();
         const float* sdl = st + TR;
@@ -912,7 +1059,7 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_summary_kernel(const MMParam
             float dti[IPL], dyi[IPL];
 #pragma unroll
             for (int i = 0; i < IPL; ++i) {
-                const int row = (w0 + ibase + i) * RP + dl;
+                const int row = Cf::dix(w0 + ibase + i, dl);
                 const float r = sdl[row] + bias_d;
                 dti[i] = SOFTPLUS ? softplus_f(r) : r;
                 float dy = sdo[row];
@@ -965,41 +1112,85 @@ __global__ void __launch_bounds__(MM_NT) mmscan_bwd_summary_kernel(const MMParam
 // ---------------------------------------------------------------------------
 // host-side launchers (instantiated per element type in separate units)
 // ---------------------------------------------------------------------------
-template <int N, int NP, bool SP, bool Z, class E, bool SUMM>
-int launch_fwd_t(const MMParams& p, cudaStream_t stream) {
+// Tensor maps of the activation and B/C tiles a launch stages; false (and the
+// kernel falls back to cp.async) when the rows are not 16-byte aligned or the
+// driver declines an encoding.
+template <int N, int NP, class E>
+bool mm_build_tmaps(const MMParams& p, MMTmaps& tm) {
     using Cf = MMCfg<N, NP>;
-    const size_t smem = sizeof(float) * MMSmem<N, NP, 3, E::BYTES>::FLOATS;
+    if (!p.vec) return false;
+    const int eb = E::BYTES;
+    const int swz = eb == 4 ? Cf::SWB : 0;  // bf16 raw tiles land unswizzled
+    struct Act { int slot; const void* ptr; int64_t s1, s0; };
+    const Act acts[4] = {{TM_X, p.x, p.xs[1], p.xs[0]},
+                         {TM_DELTA, p.delta, p.ds[1], p.ds[0]},
+                         {TM_Z, p.z, p.zs[1], p.zs[0]},
+                         {TM_DOUT, p.dout, p.D, p.L * p.D}};
+    for (const Act& a : acts) {
+        if (!a.ptr) continue;
+        if (!mmb_encode_tile_map(&tm.m[a.slot], a.ptr, eb, p.D, p.L, p.Bsz, a.s1, a.s0, Cf::DT,
+                                 MM_T, swz))
+            return false;
+    }
+    const Act bc[2] = {{TM_B, p.Bm, p.bs[1], p.bs[0]}, {TM_C, p.Cm, p.cs[1], p.cs[0]}};
+    for (const Act& a : bc) {
+        if (!a.ptr) continue;
+        if (!mmb_encode_tile_map(&tm.m[a.slot], a.ptr, eb, N, p.L, p.Bsz, a.s1, a.s0, N, MM_T, 0))
+            return false;
+    }
+    return true;
+}
+
+template <int N, int NP, class E>
+MMParams mm_launch_params(const MMParams& p0, MMTmaps& tm) {
+    MMParams p = p0;
+    p.tma = mm_build_tmaps<N, NP, E>(p, tm) ? 1 : 0;
+    p.err = mmb_device_error_flag();
+    return p;
+}
+
+template <int N, int NP, bool SP, bool Z, class E, bool SUMM>
+int launch_fwd_t(const MMParams& p0, cudaStream_t stream) {
+    using Cf = MMCfg<N, NP>;
+    const size_t smem = sizeof(float) * MMSmem<N, NP, 3, E::BYTES>::FLOATS + MM_SMEM_ALIGN;
     static int attr_done[MMB_MAX_DEVICES] = {};
     const int st = mmb_smem_attr(mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM>, smem, attr_done);
     if (st != MMB_OK) return st;
+    MMTmaps tm;
+    const MMParams p = mm_launch_params<N, NP, E>(p0, tm);
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
-    mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM><<<grid, MM_NT, smem, stream>>>(p);
+    mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM><<<grid, MM_NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }
 
 template <int N, int NP, bool SP, bool Z, class E>
-int launch_bwd_t(const MMParams& p, cudaStream_t stream) {
+int launch_bwd_t(const MMParams& p0, cudaStream_t stream) {
     using Cf = MMCfg<N, NP>;
     const size_t smem =
         sizeof(float) * (MMSmem<N, NP, 4, E::BYTES>::FLOATS + MM_CK * Cf::DT * 2 * N +
-                         (mm_bwd_cbuf<N>() ? (MM_NT / 32) * MM_T * 2 * N : 0));
+                         (mm_bwd_cbuf<N>() ? (MM_NT / 32) * MM_T * 2 * N : 0)) +
+        MM_SMEM_ALIGN;
     static int attr_done[MMB_MAX_DEVICES] = {};
     const int st = mmb_smem_attr(mmscan_bwd_kernel<N, NP, SP, Z, E>, smem, attr_done);
     if (st != MMB_OK) return st;
+    MMTmaps tm;
+    const MMParams p = mm_launch_params<N, NP, E>(p0, tm);
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
-    mmscan_bwd_kernel<N, NP, SP, Z, E><<<grid, MM_NT, smem, stream>>>(p);
+    mmscan_bwd_kernel<N, NP, SP, Z, E><<<grid, MM_NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }
 
 template <int N, int NP, bool SP, bool Z, class E>
-int launch_bwd_summary_t(const MMParams& p, cudaStream_t stream) {
+int launch_bwd_summary_t(const MMParams& p0, cudaStream_t stream) {
     using Cf = MMCfg<N, NP>;
-    const size_t smem = sizeof(float) * MMSmem<N, NP, 4, E::BYTES>::FLOATS;
+    const size_t smem = sizeof(float) * MMSmem<N, NP, 4, E::BYTES>::FLOATS + MM_SMEM_ALIGN;
     static int attr_done[MMB_MAX_DEVICES] = {};
     const int st = mmb_smem_attr(mmscan_bwd_summary_kernel<N, NP, SP, Z, E>, smem, attr_done);
     if (st != MMB_OK) return st;
+    MMTmaps tm;
+    const MMParams p = mm_launch_params<N, NP, E>(p0, tm);
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
-    mmscan_bwd_summary_kernel<N, NP, SP, Z, E><<<grid, MM_NT, smem, stream>>>(p);
+    mmscan_bwd_summary_kernel<N, NP, SP, Z, E><<<grid, MM_NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }
 

@@ -93,3 +93,10 @@ def test_noalloc_rejects_problems_beyond_the_scratch():
     st = fn(1, 4, 4, 0, _lib.ptr(M), _lib.ptr(F), None, _lib.ptr(X), _lib.stream_of(M))
     assert st == 0
     torch.cuda.synchronize()
+
+
+def test_no_device_wait_gave_up():
+    """After everything above ran, no bounded device-side wait (the TMA tile
+    pipelines' transaction barriers) reported a timeout."""
+    lib = _lib.load()
+    assert lib.mmb_device_status(_lib.stream_of(torch.empty(1, device=DEV))) == 0
