@@ -358,8 +358,11 @@ def run_b200(args):
 
 
 def run_e2e(torch, fn, dev, layers, args, steps=3):
-    """Same metric through selective_scan_momentum_fn + autograd, with inputs
-    copied in from pinned host memory and all outputs copied back every step."""
+    """Same metric through selective_scan_momentum_fn + autograd, with each
+    layer's inputs copied in from pinned host memory and all its outputs copied
+    back every step.  The copies run on two side streams so that the next
+    layer's inputs come in while the previous layer's outputs go out (PCIe is
+    full duplex); the scans run on the current stream in layer order."""
     host_in, host_out = [], []
     for ly in layers:
         host_in.append({k: getattr(ly, k).cpu().pin_memory()
@@ -369,10 +372,29 @@ def run_e2e(torch, fn, dev, layers, args, steps=3):
     A, D, bias = layers[0].A, layers[0].D, layers[0].bias
     h2d = sum(t.numel() * 4 for t in host_in[0].values()) * LAYERS
     d2h = sum(t.numel() * 4 for t in host_out[0].values()) * LAYERS
+    comp = torch.cuda.current_stream(dev)
+    s_in = torch.cuda.Stream(device=dev)
+    s_out = torch.cuda.Stream(device=dev)
 
     def one():
-        for hi, ho in zip(host_in, host_out):
-            d = {k: v.to(dev, non_blocking=True) for k, v in hi.items()}
+        dev_in = [None] * LAYERS
+        s_in.wait_stream(comp)  # the step's copies start after the previous step
+
+        def fetch(i):
+            with torch.cuda.stream(s_in):
+                dev_in[i] = {k: v.to(dev, non_blocking=True) for k, v in host_in[i].items()}
+                ev = torch.cuda.Event()
+                ev.record(s_in)
+            return ev
+
+        ready = fetch(0)
+        for i in range(LAYERS):
+            comp.wait_event(ready)
+            d = dev_in[i]
+            for t in d.values():
+                t.record_stream(comp)
+            if i + 1 < LAYERS:
+                ready = fetch(i + 1)
             ins = [d["x"].requires_grad_(True), d["delta"].requires_grad_(True),
                    A.detach().requires_grad_(True), d["B"].requires_grad_(True),
                    d["C"].requires_grad_(True), D.detach().requires_grad_(True),
@@ -380,23 +402,33 @@ def run_e2e(torch, fn, dev, layers, args, steps=3):
             y = fn(ins[0], ins[1], ins[2], ins[3], ins[4], ins[5], z=ins[6], delta_bias=ins[7],
                    delta_softplus=True, beta=BETA, alpha=ALPHA)
             gx, gd, gA, gB, gC, gD, gz, gb = torch.autograd.grad(y, ins, d["dout"])
-            for k, v in (("out", y), ("dx", gx), ("ddelta", gd), ("dz", gz), ("dB", gB),
-                         ("dC", gC), ("dA", gA), ("dD", gD), ("dbias", gb)):
-                ho[k].copy_(v.detach(), non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(comp)
+            outs = (("out", y), ("dx", gx), ("ddelta", gd), ("dz", gz), ("dB", gB), ("dC", gC),
+                    ("dA", gA), ("dD", gD), ("dbias", gb))
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(done)
+                for k, v in outs:
+                    v = v.detach()
+                    v.record_stream(s_out)
+                    host_out[i][k].copy_(v, non_blocking=True)
+        comp.wait_stream(s_out)
 
     one()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
+    e0.record(comp)
     for _ in range(steps):
         one()
-    e1.record()
+    e1.record(comp)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     return {"value": ELEMS_PER_LAYER * LAYERS / (ms / 1e3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
-            "steps": steps, "api": "selective_scan_momentum_fn + torch.autograd.grad"}
+            "steps": steps, "api": "selective_scan_momentum_fn + torch.autograd.grad",
+            "copies": "pinned host buffers; inputs of layer i+1 in while outputs of layer i "
+                      "go out (two copy streams)"}
 
 
 # ---------------------------------------------------------------------------
@@ -642,6 +674,136 @@ def run_long(args):
     }
 
 
+# ---------------------------------------------------------------------------
+# LinOSS layer scan workload (IM and IMEX discretisations)
+# ---------------------------------------------------------------------------
+LINOSS = dict(batch=16, seqlen=4096, osc=256)
+
+
+def run_linoss(args):
+    """The LinOSS layer scan (LinOSS_pytorch.py:153-239, time-invariant 2x2
+    transition built in-kernel) forward + backward for IM and IMEX at B=16
+    L=4096 P=256 with complex Bu ~ N(0,1), A ~ U[0,1], step = exp(U[ln 1e-3,
+    ln 1e-1]).  One step = IM fwd + bwd and IMEX fwd + bwd; elements = B L P
+    oscillator steps per discretisation.  Batch-sharded over ranks (weak)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from momentummamba_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+    Bsz, L, P = LINOSS["batch"], LINOSS["seqlen"], LINOSS["osc"]
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    A = torch.rand(P, device=dev, generator=g)
+    step = torch.exp(torch.rand(P, device=dev, generator=g) * (math.log(0.1) - math.log(1e-3))
+                     + math.log(1e-3))
+    Bu = torch.randn(Bsz, L, P, 2, device=dev, generator=g)
+    dx2 = torch.randn(Bsz, L, P, 2, device=dev, generator=g)
+    x2 = torch.empty_like(Bu)
+    dBu = torch.empty_like(Bu)
+    dA = torch.empty_like(A)
+    ds = torch.empty_like(step)
+    works = [torch.empty(lib.mmb_linoss_work_floats(Bsz, L, P), device=dev) for _ in range(2)]
+    Pp = _lib.ptr
+    s = _lib.stream_of(Bu)
+
+    def fwd(disc):
+        _lib.check(lib.mmb_linoss_fwd(disc, Bsz, L, P, Pp(A), Pp(step), Pp(Bu), Pp(x2),
+                                      Pp(works[disc]), s), "linoss fwd")
+
+    def bwd(disc):
+        _lib.check(lib.mmb_linoss_bwd(disc, Bsz, L, P, Pp(A), Pp(step), Pp(Bu), Pp(dx2), Pp(dBu),
+                                      Pp(dA), Pp(ds), Pp(works[disc]), s), "linoss bwd")
+
+    def stepfn():
+        for disc in (0, 1):   # IM, IMEX
+            fwd(disc)
+            bwd(disc)
+
+    for _ in range(max(3, args.warmup)):
+        stepfn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(device=dev)
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(graph, stream=cs):
+            stepfn()
+    torch.cuda.current_stream().wait_stream(cs)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    # per-kernel durations
+    reps = 10
+    t = {}
+    cur = torch.cuda.current_stream()
+    for name, fn in (("fwd_IM", lambda: fwd(0)), ("bwd_IM", lambda: bwd(0)),
+                     ("fwd_IMEX", lambda: fwd(1)), ("bwd_IMEX", lambda: bwd(1))):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for a, b in evs:
+            a.record(cur)
+            fn()
+            b.record(cur)
+        torch.cuda.synchronize()
+        t[name] = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    del graph
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    elems = Bsz * L * P
+    fwd_b = elems * 16 + 2 * P * 4          # read Bu, write x2 (complex fp32)
+    bwd_b = elems * 24 + 4 * P * 4          # read Bu, dx2; write dBu
+    peak, peak_kind = load_peaks()
+    achieved = bwd_b / (t["bwd_IM"] / 1e3) / 1e9
+    return {
+        "metric": METRIC, "value": job_rate(2 * elems * args.steps, world, ms), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "LinOSS layer scan fwd+bwd, IM and IMEX: B=16 L=4096 P=256, "
+                               "complex Bu ~ N(0,1), A ~ U[0,1], step = exp(U[ln 1e-3, ln 1e-1]); "
+                               "elements = B*L*P oscillator steps per discretisation",
+                   "parallelism": f"batch-sharded x{world}", "launch": "cuda graph",
+                   "l2": "inputs larger than L2 (Bu, dx2 268 MB each)"},
+        "roofline": {"kernel": "lin_bwd (IM)", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": achieved / peak,
+                     "algorithmic_bytes": bwd_b, "ms_per_launch": t["bwd_IM"], "traffic": None},
+        "kernels": {k: {"ms": v, "algorithmic_bytes": fwd_b if k.startswith("fwd") else bwd_b,
+                        "GB/s": (fwd_b if k.startswith("fwd") else bwd_b) / (v / 1e3) / 1e9}
+                    for k, v in t.items()},
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -656,9 +818,10 @@ def main():
                     help="run warm-up and steps eagerly and exit (for profiler captures)")
     ap.add_argument("--batch", type=int, default=BSZ,
                     help="sequences per layer (profiling only; the benchmark line uses 32)")
-    ap.add_argument("--workload", choices=["stack", "long"], default="stack",
+    ap.add_argument("--workload", choices=["stack", "long", "linoss"], default="stack",
                     help="stack: the 4-layer MambaMomentum scan (batch-sharded, the benchmark "
-                         "line); long: B=8 L=65536 D=2048 bf16, sequence-sharded")
+                         "line); long: B=8 L=65536 D=2048 bf16, sequence-sharded; linoss: the "
+                         "LinOSS layer scan, IM and IMEX, B=16 L=4096 P=256")
     ap.add_argument("--phases", action="store_true",
                     help="long workload: also time each phase (adds events to the step)")
     args = ap.parse_args()
@@ -667,6 +830,8 @@ def main():
         line = run_reference(args)
     elif args.workload == "long":
         line = run_long(args)
+    elif args.workload == "linoss":
+        line = run_linoss(args)
     else:
         line = run_b200(args)
     if line is not None:
