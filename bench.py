@@ -714,15 +714,15 @@ def run_linoss(args):
     ds = torch.empty_like(step)
     works = [torch.empty(lib.mmb_linoss_work_floats(Bsz, L, P), device=dev) for _ in range(2)]
     Pp = _lib.ptr
-    s = _lib.stream_of(Bu)
 
-    def fwd(disc):
+    def fwd(disc):  # on the current stream (the capture stream while capturing)
         _lib.check(lib.mmb_linoss_fwd(disc, Bsz, L, P, Pp(A), Pp(step), Pp(Bu), Pp(x2),
-                                      Pp(works[disc]), s), "linoss fwd")
+                                      Pp(works[disc]), _lib.stream_of(Bu)), "linoss fwd")
 
     def bwd(disc):
         _lib.check(lib.mmb_linoss_bwd(disc, Bsz, L, P, Pp(A), Pp(step), Pp(Bu), Pp(dx2), Pp(dBu),
-                                      Pp(dA), Pp(ds), Pp(works[disc]), s), "linoss bwd")
+                                      Pp(dA), Pp(ds), Pp(works[disc]), _lib.stream_of(Bu)),
+                   "linoss bwd")
 
     def stepfn():
         for disc in (0, 1):   # IM, IMEX

@@ -412,6 +412,28 @@ __device__ __forceinline__ float2 ld_bu(const float* base, int64_t Bsz, int64_t 
     return __ldg(reinterpret_cast<const float2*>(base) + (b * L + t) * P + j);
 }
 
+// The time loops below work in 8-step windows: a window's inputs are loaded
+// into registers before its dependent recurrence runs (the stores of a window
+// would otherwise pin every later load behind them), and the carry passes
+// prefetch 8 chunk records at a time.
+__device__ __forceinline__ void lin_step(const LinCoef& k, float2 u, float& x1r, float& x1i,
+                                         float& x2r, float& x2i) {
+    const float n1r = k.m.a * x1r + k.m.b * x2r + k.f1 * u.x;
+    const float n1i = k.m.a * x1i + k.m.b * x2i + k.f1 * u.y;
+    const float n2r = k.m.c * x1r + k.m.d * x2r + k.f2 * u.x;
+    const float n2i = k.m.c * x1i + k.m.d * x2i + k.f2 * u.y;
+    x1r = n1r; x1i = n1i; x2r = n2r; x2i = n2i;
+}
+
+// the window [ws, ws + 8) of a chain's (B, L, P) complex sequence, zeros past t1
+__device__ __forceinline__ void lin_load_window(const float* __restrict__ base, const LinParams& q,
+                                                int64_t b, int64_t ws, int64_t t1, int64_t j,
+                                                float2 (&u)[S2_CK]) {
+    const float2* r = reinterpret_cast<const float2*>(base) + (b * q.L + ws) * q.P + j;
+#pragma unroll
+    for (int s = 0; s < S2_CK; ++s) u[s] = ws + s < t1 ? __ldg(r + s * q.P) : make_float2(0.f, 0.f);
+}
+
 __global__ void __launch_bounds__(S2_NT) lin_fwd_summary(const LinParams q) {
     const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
     if (idx >= q.Bsz * q.C * q.P) return;
@@ -419,13 +441,12 @@ __global__ void __launch_bounds__(S2_NT) lin_fwd_summary(const LinParams q) {
     const int64_t t0 = c * q.T, t1 = min64(q.L, t0 + q.T);
     const LinCoef k = lin_coef(q.disc, q.A[j], q.step[j]);
     float x1r = 0.f, x1i = 0.f, x2r = 0.f, x2i = 0.f;
-    for (int64_t t = t0; t < t1; ++t) {
-        const float2 u = ld_bu(q.Bu, q.Bsz, q.L, q.P, b, t, j);
-        const float n1r = k.m.a * x1r + k.m.b * x2r + k.f1 * u.x;
-        const float n1i = k.m.a * x1i + k.m.b * x2i + k.f1 * u.y;
-        const float n2r = k.m.c * x1r + k.m.d * x2r + k.f2 * u.x;
-        const float n2i = k.m.c * x1i + k.m.d * x2i + k.f2 * u.y;
-        x1r = n1r; x1i = n1i; x2r = n2r; x2i = n2i;
+    for (int64_t ws = t0; ws < t1; ws += S2_CK) {
+        float2 u[S2_CK];
+        lin_load_window(q.Bu, q, b, ws, t1, j, u);
+#pragma unroll
+        for (int s = 0; s < S2_CK; ++s)
+            if (ws + s < t1) lin_step(k, u[s], x1r, x1i, x2r, x2i);
     }
     reinterpret_cast<float4*>(lin_summ(q))[idx] = make_float4(x1r, x1i, x2r, x2i);
 }
@@ -438,15 +459,21 @@ __global__ void __launch_bounds__(S2_NT) lin_fwd_carry(const LinParams q) {
     Mat2 mT = mident();  // M^T, the transition over a full chunk
     for (int64_t s = 0; s < q.T; ++s) mT = mmul(k.m, mT);
     float x1r = 0.f, x1i = 0.f, x2r = 0.f, x2i = 0.f;
-    const float4* summ = reinterpret_cast<const float4*>(lin_summ(q));
-    float4* carry = reinterpret_cast<float4*>(lin_carry(q));
-    for (int64_t c = 0; c < q.C; ++c) {
-        const int64_t r = (b * q.C + c) * q.P + j;
-        carry[r] = make_float4(x1r, x1i, x2r, x2i);
-        const float4 s = summ[r];
-        mvec(mT, x1r, x2r);
-        mvec(mT, x1i, x2i);
-        x1r += s.x; x1i += s.y; x2r += s.z; x2i += s.w;
+    const float4* __restrict__ summ = reinterpret_cast<const float4*>(lin_summ(q));
+    float4* __restrict__ carry = reinterpret_cast<float4*>(lin_carry(q));
+    for (int64_t c0 = 0; c0 < q.C; c0 += 8) {
+        float4 sv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            sv[i] = c0 + i < q.C ? summ[(b * q.C + c0 + i) * q.P + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (c0 + i >= q.C) break;
+            carry[(b * q.C + c0 + i) * q.P + j] = make_float4(x1r, x1i, x2r, x2i);
+            mvec(mT, x1r, x2r);
+            mvec(mT, x1i, x2i);
+            x1r += sv[i].x; x1i += sv[i].y; x2r += sv[i].z; x2i += sv[i].w;
+        }
     }
 }
 
@@ -458,17 +485,18 @@ __global__ void __launch_bounds__(S2_NT) lin_fwd_final(const LinParams q) {
     const LinCoef k = lin_coef(q.disc, q.A[j], q.step[j]);
     const float4 in = reinterpret_cast<const float4*>(lin_carry(q))[idx];
     float x1r = in.x, x1i = in.y, x2r = in.z, x2i = in.w;
-    float4* ck = reinterpret_cast<float4*>(lin_ckpt(q));
-    float2* xo = reinterpret_cast<float2*>(q.x2);
-    for (int64_t t = t0; t < t1; ++t) {
-        if (t % S2_CK == 0 && ck) ck[(b * q.K + t / S2_CK) * q.P + j] = make_float4(x1r, x1i, x2r, x2i);
-        const float2 u = ld_bu(q.Bu, q.Bsz, q.L, q.P, b, t, j);
-        const float n1r = k.m.a * x1r + k.m.b * x2r + k.f1 * u.x;
-        const float n1i = k.m.a * x1i + k.m.b * x2i + k.f1 * u.y;
-        const float n2r = k.m.c * x1r + k.m.d * x2r + k.f2 * u.x;
-        const float n2i = k.m.c * x1i + k.m.d * x2i + k.f2 * u.y;
-        x1r = n1r; x1i = n1i; x2r = n2r; x2i = n2i;
-        xo[(b * q.L + t) * q.P + j] = make_float2(x2r, x2i);
+    float4* __restrict__ ck = reinterpret_cast<float4*>(lin_ckpt(q));
+    float2* __restrict__ xo = reinterpret_cast<float2*>(q.x2) + b * q.L * q.P + j;
+    for (int64_t ws = t0; ws < t1; ws += S2_CK) {  // ws is a multiple of 8
+        float2 u[S2_CK];
+        lin_load_window(q.Bu, q, b, ws, t1, j, u);
+        if (ck) ck[(b * q.K + ws / S2_CK) * q.P + j] = make_float4(x1r, x1i, x2r, x2i);
+#pragma unroll
+        for (int s = 0; s < S2_CK; ++s) {
+            if (ws + s >= t1) break;
+            lin_step(k, u[s], x1r, x1i, x2r, x2i);
+            xo[(ws + s) * q.P] = make_float2(x2r, x2i);
+        }
     }
 }
 
@@ -480,14 +508,21 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_summary(const LinParams q) {
     const int64_t t0 = c * q.T, t1 = min64(q.L, t0 + q.T);
     const Mat2 mt = mtrans(lin_coef(q.disc, q.A[j], q.step[j]).m);
     float l1r = 0.f, l1i = 0.f, l2r = 0.f, l2i = 0.f;
-    for (int64_t t = t1 - 1; t >= t0; --t) {
-        if (t < t1 - 1) {
-            mvec(mt, l1r, l2r);
-            mvec(mt, l1i, l2i);
+    bool first = true;
+    for (int64_t ws = t0 + (t1 - 1 - t0) / S2_CK * S2_CK; ws >= t0; ws -= S2_CK) {
+        float2 g[S2_CK];
+        lin_load_window(q.dx2, q, b, ws, t1, j, g);
+#pragma unroll
+        for (int s = S2_CK - 1; s >= 0; --s) {
+            if (ws + s >= t1) continue;
+            if (!first) {
+                mvec(mt, l1r, l2r);
+                mvec(mt, l1i, l2i);
+            }
+            first = false;
+            l2r += g[s].x;
+            l2i += g[s].y;
         }
-        const float2 g = ld_bu(q.dx2, q.Bsz, q.L, q.P, b, t, j);
-        l2r += g.x;
-        l2i += g.y;
     }
     reinterpret_cast<float4*>(lin_summ(q))[idx] = make_float4(l1r, l1i, l2r, l2i);
 }
@@ -502,17 +537,23 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_carry(const LinParams q) {
     Mat2 pw = mident();
     for (int64_t s = 1; s < q.T; ++s) pw = mmul(mt, pw);
     float m1r = 0.f, m1i = 0.f, m2r = 0.f, m2i = 0.f;
-    const float4* summ = reinterpret_cast<const float4*>(lin_summ(q));
-    float4* carry = reinterpret_cast<float4*>(lin_carry(q));
-    for (int64_t c = q.C - 1; c >= 0; --c) {
-        const int64_t r = (b * q.C + c) * q.P + j;
-        carry[r] = make_float4(m1r, m1i, m2r, m2i);
-        mvec(pw, m1r, m2r);
-        mvec(pw, m1i, m2i);
-        const float4 l = summ[r];
-        m1r += l.x; m1i += l.y; m2r += l.z; m2i += l.w;
-        mvec(mt, m1r, m2r);
-        mvec(mt, m1i, m2i);
+    const float4* __restrict__ summ = reinterpret_cast<const float4*>(lin_summ(q));
+    float4* __restrict__ carry = reinterpret_cast<float4*>(lin_carry(q));
+    for (int64_t c0 = q.C - 1; c0 >= 0; c0 -= 8) {
+        float4 sv[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            sv[i] = c0 - i >= 0 ? summ[(b * q.C + c0 - i) * q.P + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            if (c0 - i < 0) break;
+            carry[(b * q.C + c0 - i) * q.P + j] = make_float4(m1r, m1i, m2r, m2i);
+            mvec(pw, m1r, m2r);
+            mvec(pw, m1i, m2i);
+            m1r += sv[i].x; m1i += sv[i].y; m2r += sv[i].z; m2i += sv[i].w;
+            mvec(mt, m1r, m2r);
+            mvec(mt, m1i, m2i);
+        }
     }
 }
 
@@ -532,34 +573,27 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_final(const LinParams q) {
         const Mat2 mt = mtrans(k.m);
         const float4 mu = reinterpret_cast<const float4*>(lin_carry(q))[idx];
         float l1r = mu.x, l1i = mu.y, l2r = mu.z, l2i = mu.w;  // M^T lambda_{t+1}
-        const float4* ck = reinterpret_cast<const float4*>(lin_ckpt(q));
-        float2* dbu = reinterpret_cast<float2*>(q.dBu);
-        // windows of the checkpoint grid that overlap [t0, t1)
-        const int64_t wlast = (t1 - 1) / S2_CK, wfirst = t0 / S2_CK;
-        for (int64_t w = wlast; w >= wfirst; --w) {
-            const int64_t ws = w * S2_CK;
-            const float4 x0 = ck[(b * q.K + w) * q.P + j];
+        const float4* __restrict__ ck = reinterpret_cast<const float4*>(lin_ckpt(q));
+        float2* __restrict__ dbu = reinterpret_cast<float2*>(q.dBu) + b * q.L * q.P + j;
+        // windows [ws, ws + 8) of the chunk (t0 and T are multiples of 8)
+        for (int64_t ws = t0 + (t1 - 1 - t0) / S2_CK * S2_CK; ws >= t0; ws -= S2_CK) {
+            float2 us[S2_CK], gs[S2_CK];
+            lin_load_window(q.Bu, q, b, ws, t1, j, us);
+            lin_load_window(q.dx2, q, b, ws, t1, j, gs);
+            const float4 x0 = ck[(b * q.K + ws / S2_CK) * q.P + j];
             float xs[S2_CK + 1][4];
             xs[0][0] = x0.x; xs[0][1] = x0.y; xs[0][2] = x0.z; xs[0][3] = x0.w;
-            float2 us[S2_CK];
 #pragma unroll
             for (int s = 0; s < S2_CK; ++s) {
-                const int64_t t = ws + s;
-                const float2 u = t < q.L ? ld_bu(q.Bu, q.Bsz, q.L, q.P, b, t, j) : make_float2(0.f, 0.f);
-                us[s] = u;
-                xs[s + 1][0] = k.m.a * xs[s][0] + k.m.b * xs[s][2] + k.f1 * u.x;
-                xs[s + 1][1] = k.m.a * xs[s][1] + k.m.b * xs[s][3] + k.f1 * u.y;
-                xs[s + 1][2] = k.m.c * xs[s][0] + k.m.d * xs[s][2] + k.f2 * u.x;
-                xs[s + 1][3] = k.m.c * xs[s][1] + k.m.d * xs[s][3] + k.f2 * u.y;
+                xs[s + 1][0] = xs[s][0]; xs[s + 1][1] = xs[s][1];
+                xs[s + 1][2] = xs[s][2]; xs[s + 1][3] = xs[s][3];
+                lin_step(k, us[s], xs[s + 1][0], xs[s + 1][1], xs[s + 1][2], xs[s + 1][3]);
             }
 #pragma unroll
             for (int s = S2_CK - 1; s >= 0; --s) {
-                const int64_t t = ws + s;
-                if (t < t0 || t >= t1) continue;
-                const float2 gx = ld_bu(q.dx2, q.Bsz, q.L, q.P, b, t, j);
-                const float a1r = l1r, a1i = l1i, a2r = l2r + gx.x, a2i = l2i + gx.y;  // lambda_t
-                dbu[(b * q.L + t) * q.P + j] =
-                    make_float2(k.f1 * a1r + k.f2 * a2r, k.f1 * a1i + k.f2 * a2i);
+                if (ws + s >= t1) continue;
+                const float a1r = l1r, a1i = l1i, a2r = l2r + gs[s].x, a2i = l2i + gs[s].y;
+                dbu[(ws + s) * q.P] = make_float2(k.f1 * a1r + k.f2 * a2r, k.f1 * a1i + k.f2 * a2i);
                 // state before step t (zero at t = 0: the checkpoint there is zero)
                 g[0] += a1r * xs[s][0] + a1i * xs[s][1];
                 g[1] += a1r * xs[s][2] + a1i * xs[s][3];
@@ -641,11 +675,15 @@ static size_t s2_work(int64_t Bsz, int64_t L, int64_t P, int nc) {
     return (size_t)(fwd > bwd ? fwd : bwd);
 }
 
+// Chunks of the LinOSS layer scan are whole 8-step windows, so chunk,
+// window and checkpoint boundaries coincide.
 static void lin_dims(int64_t Bsz, int64_t L, int64_t P, LinParams& q) {
     q.Bsz = Bsz;
     q.L = L;
     q.P = P;
     s2_chunks(Bsz, L, P, q.T, q.C);
+    q.T = (q.T + S2_CK - 1) / S2_CK * S2_CK;
+    q.C = (L + q.T - 1) / q.T;
     q.K = (L + S2_CK - 1) / S2_CK;
 }
 
