@@ -378,6 +378,35 @@ int mmb_linoss_bwd(int32_t disc, int64_t batch, int64_t L, int64_t P, const floa
                    const float* step, const float* Bu, const float* dx2, float* dBu,
                    float* dA_diag, float* dstep, float* work, mmb_stream_t stream);
 
+/* =========================================================================
+ * Selective LinOSS scan of the Mamba-LinOSS block, fused
+ * (apply_linoss_vectorized, mamba_linoss.py:608-677): per step the transition
+ * and input scale are built from s[b,t] (= mean over channels of delta) and
+ * A_diag[p], and the output contraction is done in the kernel:
+ *   IM:   S = 1/(1 + s^2 A); M = [[S, -s A S], [s S, S]]; F = (s S B, s^2 S B)
+ *   IMEX: M = [[1, -s A], [s, 1 - s^2 A]];               F = (s B, s^2 B)
+ *   x_t = M_t x_{t-1} + F_t (complex, x_{-1} = 0);  y[b,t] = Re sum_p C x2
+ * B_re, B_im, C_re, C_im: (batch, L, P) with (batch, seq) strides B_stride /
+ * C_stride shared by each re/im pair, unit stride along P; s, y, dy, ds
+ * (batch, L) contiguous; A_diag, dA_diag (P).  The backward writes dB_re,
+ * dB_im, dC_re, dC_im ((batch, L, P) contiguous) and the sums dA_diag and ds.
+ * `work`: mmb_linoss_sel_work_floats(batch, L, P) floats, 16-byte aligned; the
+ * backward needs its forward's work buffer unchanged.
+ * ========================================================================= */
+size_t mmb_linoss_sel_work_floats(int64_t batch, int64_t L, int64_t P);
+
+int mmb_linoss_sel_fwd(int32_t disc, int64_t batch, int64_t L, int64_t P, const float* A_diag,
+                       const float* s, const float* B_re, const float* B_im,
+                       const int64_t* B_stride, const float* C_re, const float* C_im,
+                       const int64_t* C_stride, float* y, float* work, mmb_stream_t stream);
+
+int mmb_linoss_sel_bwd(int32_t disc, int64_t batch, int64_t L, int64_t P, const float* A_diag,
+                       const float* s, const float* B_re, const float* B_im,
+                       const int64_t* B_stride, const float* C_re, const float* C_im,
+                       const int64_t* C_stride, const float* dy, float* dB_re, float* dB_im,
+                       float* dC_re, float* dC_im, float* dA_diag, float* ds, float* work,
+                       mmb_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -83,6 +83,11 @@ _SIGNATURES = {
                             + [_c_p] * 8),
     "mmb_conv1d_step": (ctypes.c_int, [_c_i64, _c_i64, _c_i32, _c_p, _c_i64] + [_c_p] * 6),
     "mmb_mmscan_step": (ctypes.c_int, [ctypes.POINTER(StepDesc)] + [_c_p] * 14),
+    "mmb_linoss_sel_work_floats": (_c_size, [_c_i64, _c_i64, _c_i64]),
+    "mmb_linoss_sel_fwd": (ctypes.c_int, [_c_i32, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p,
+                                          _I64_P, _c_p, _c_p, _I64_P, _c_p, _c_p, _c_p]),
+    "mmb_linoss_sel_bwd": (ctypes.c_int, [_c_i32, _c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p,
+                                          _I64_P, _c_p, _c_p, _I64_P] + [_c_p] * 9),
     "mmb_rows_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p]),
     "mmb_rows_bwd": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_p, _c_f, _c_p, _c_p, _c_p, _c_p]),
     "mmb_pscan_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_p, _c_p, _c_p, _c_p]),

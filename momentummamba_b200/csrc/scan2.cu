@@ -91,6 +91,11 @@ constexpr int S2_REC = 8;  // floats per (b, chunk, p) record of each table (2*n
 // ---------------------------------------------------------------------------
 // generic forward
 // ---------------------------------------------------------------------------
+// The time loops work in windows of S2_W steps: a window's inputs are loaded
+// before its dependent recurrence and stores (which would otherwise hold
+// every later load behind them); the carry passes prefetch S2_W chunk records.
+constexpr int S2_W = 4;
+
 template <int NC, bool MSCAN>
 __global__ void __launch_bounds__(S2_NT) s2_fwd_summary(const S2Params p) {
     const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
@@ -132,26 +137,33 @@ __global__ void __launch_bounds__(S2_NT) s2_fwd_carry(const S2Params p) {
 #pragma unroll
     for (int k = 0; k < NC; ++k) x1[k] = x2[k] = 0.f;
     Mat2 pre = mident();
-    const float* summ = p.work;
-    float* carry = p.work + p.Bsz * p.C * p.P * S2_REC;
-    for (int64_t c = 0; c < p.C; ++c) {
-        const int64_t r = (b * p.C + c) * p.P + j;
-        float* out = carry + r * S2_REC;
-        out[0] = pre.a; out[1] = pre.b; out[2] = pre.c; out[3] = pre.d;
+    const float* __restrict__ summ = p.work;
+    float* __restrict__ carry = p.work + p.Bsz * p.C * p.P * S2_REC;
+    for (int64_t c0 = 0; c0 < p.C; c0 += S2_W) {
+        float4 sm[S2_W], sx[S2_W];  // the records: [Mprod | x_loc]
 #pragma unroll
-        for (int k = 0; k < NC; ++k) {
-            out[4 + 2 * k] = x1[k];
-            out[5 + 2 * k] = x2[k];
+        for (int i = 0; i < S2_W; ++i) {  // records past the end: the last one again (unused)
+            const int64_t ci = c0 + i < p.C ? c0 + i : p.C - 1;
+            const float4* r = reinterpret_cast<const float4*>(summ + ((b * p.C + ci) * p.P + j) * S2_REC);
+            sm[i] = r[0];
+            sx[i] = r[1];
         }
-        const float* s = summ + r * S2_REC;
-        const Mat2 mc = {s[0], s[1], s[2], s[3]};
 #pragma unroll
-        for (int k = 0; k < NC; ++k) {
-            mvec(mc, x1[k], x2[k]);
-            x1[k] += s[4 + 2 * k];
-            x2[k] += s[5 + 2 * k];
+        for (int i = 0; i < S2_W; ++i) {
+            if (c0 + i >= p.C) break;
+            float4* out = reinterpret_cast<float4*>(carry + ((b * p.C + c0 + i) * p.P + j) * S2_REC);
+            out[0] = make_float4(pre.a, pre.b, pre.c, pre.d);
+            out[1] = make_float4(x1[0], x2[0], NC > 1 ? x1[NC - 1] : 0.f, NC > 1 ? x2[NC - 1] : 0.f);
+            const Mat2 mc = {sm[i].x, sm[i].y, sm[i].z, sm[i].w};
+            const float sl[4] = {sx[i].x, sx[i].y, sx[i].z, sx[i].w};
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                mvec(mc, x1[k], x2[k]);
+                x1[k] += sl[2 * k];
+                x2[k] += sl[2 * k + 1];
+            }
+            if (MSCAN) pre = mmul(mc, pre);
         }
-        if (MSCAN) pre = mmul(mc, pre);
     }
 }
 
@@ -235,20 +247,32 @@ __global__ void __launch_bounds__(S2_NT) s2_bwd_summary(const S2Params p) {
     for (int k = 0; k < NV; ++k) l1[k] = l2[k] = 0.f;
     Mat2 q = mident();  // M_{t+1}^T ... M_{t1-1}^T
     Mat2 mn = {0.f, 0.f, 0.f, 0.f};  // M_{t+1}; none past the chunk end
-    for (int64_t t = t1 - 1; t >= t0; --t) {
-        float g1[NV], g2[NV];
-        s2_gvec<NC, GMS>(p, b, t, j, g1, g2);
-        const Mat2 mt = mtrans(mn);
+    for (int64_t te = t1; te > t0; te -= S2_W) {  // window [te - S2_W, te)
+        float g1[S2_W][NV], g2[S2_W][NV];
+        Mat2 mw[S2_W];
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-            float a = l1[k], bb = l2[k];
-            mvec(mt, a, bb);
-            l1[k] = a + g1[k];
-            l2[k] = bb + g2[k];
+        for (int s = 0; s < S2_W; ++s) {
+            const int64_t t = te - 1 - s;
+            if (t >= t0) {
+                s2_gvec<NC, GMS>(p, b, t, j, g1[s], g2[s]);
+                mw[s] = load_m(p, b, t, j);
+            }
         }
-        const Mat2 m = load_m(p, b, t, j);
-        if (t > t0) q = mmul(mtrans(m), q);
-        mn = m;
+#pragma unroll
+        for (int s = 0; s < S2_W; ++s) {
+            const int64_t t = te - 1 - s;
+            if (t < t0) break;
+            const Mat2 mt = mtrans(mn);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                float a = l1[k], bb = l2[k];
+                mvec(mt, a, bb);
+                l1[k] = a + g1[s][k];
+                l2[k] = bb + g2[s][k];
+            }
+            if (t > t0) q = mmul(mtrans(mw[s]), q);
+            mn = mw[s];
+        }
     }
     float* rec = p.work + idx * Q::SREC;
 #pragma unroll
@@ -270,28 +294,39 @@ __global__ void __launch_bounds__(S2_NT) s2_bwd_carry(const S2Params p) {
     float m1[NV], m2[NV];
 #pragma unroll
     for (int k = 0; k < NV; ++k) m1[k] = m2[k] = 0.f;
-    const float* summ = p.work;
-    float* mu = p.work + p.Bsz * p.C * p.P * Q::SREC;
-    for (int64_t c = p.C - 1; c >= 0; --c) {
-        const int64_t r = (b * p.C + c) * p.P + j;
-        float* out = mu + r * Q::MREC;
+    const float* __restrict__ summ = p.work;
+    float* __restrict__ mu = p.work + p.Bsz * p.C * p.P * Q::SREC;
+    for (int64_t c0 = p.C - 1; c0 >= 0; c0 -= S2_W) {
+        float rs[S2_W][Q::SREC];
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-            out[2 * k] = m1[k];
-            out[2 * k + 1] = m2[k];
+        for (int i = 0; i < S2_W; ++i) {  // records before the start: chunk 0 again (unused)
+            const int64_t ci = c0 - i >= 0 ? c0 - i : 0;
+            const float* s = summ + ((b * p.C + ci) * p.P + j) * Q::SREC;
+#pragma unroll
+            for (int e = 0; e < Q::SREC; ++e) rs[i][e] = s[e];
         }
-        const float* s = summ + r * Q::SREC;
-        const Mat2 q = {s[2 * NV], s[2 * NV + 1], s[2 * NV + 2], s[2 * NV + 3]};
-        const Mat2 mt0 = mtrans(Mat2{s[2 * NV + 4], s[2 * NV + 5], s[2 * NV + 6], s[2 * NV + 7]});
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-            float a = m1[k], bb = m2[k];
-            mvec(q, a, bb);
-            a += s[2 * k];
-            bb += s[2 * k + 1];
-            mvec(mt0, a, bb);  // mu for the previous chunk
-            m1[k] = a;
-            m2[k] = bb;
+        for (int i = 0; i < S2_W; ++i) {
+            if (c0 - i < 0) break;
+            float* out = mu + ((b * p.C + c0 - i) * p.P + j) * Q::MREC;
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                out[2 * k] = m1[k];
+                out[2 * k + 1] = m2[k];
+            }
+            const float* s = rs[i];
+            const Mat2 q = {s[2 * NV], s[2 * NV + 1], s[2 * NV + 2], s[2 * NV + 3]};
+            const Mat2 mt0 = mtrans(Mat2{s[2 * NV + 4], s[2 * NV + 5], s[2 * NV + 6], s[2 * NV + 7]});
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                float a = m1[k], bb = m2[k];
+                mvec(q, a, bb);
+                a += s[2 * k];
+                bb += s[2 * k + 1];
+                mvec(mt0, a, bb);  // mu for the previous chunk
+                m1[k] = a;
+                m2[k] = bb;
+            }
         }
     }
 }
@@ -311,49 +346,65 @@ __global__ void __launch_bounds__(S2_NT) s2_bwd_final(const S2Params p) {
         l1[k] = mu[2 * k];
         l2[k] = mu[2 * k + 1];
     }
-    for (int64_t t = t1 - 1; t >= t0; --t) {
-        float g1[NV], g2[NV];
-        s2_gvec<NC, GMS>(p, b, t, j, g1, g2);
+    for (int64_t te = t1; te > t0; te -= S2_W) {  // window [te - S2_W, te), backwards
+        float g1[S2_W][NV], g2[S2_W][NV];
+        float xp1[S2_W][NC], xp2[S2_W][NC];  // state before the step
+        Mat2 mw[S2_W], pcw[S2_W];
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-            l1[k] += g1[k];
-            l2[k] += g2[k];
-        }
-        // dF_t = lambda_t ; dM_t = sum over channels lambda_t (x) state_{t-1}
-        float d11 = 0.f, d12 = 0.f, d21 = 0.f, d22 = 0.f;
+        for (int s = 0; s < S2_W; ++s) {
+            const int64_t t = te - 1 - s;
+            if (t < t0) continue;
+            s2_gvec<NC, GMS>(p, b, t, j, g1[s], g2[s]);
+            mw[s] = load_m(p, b, t, j);
 #pragma unroll
-        for (int k = 0; k < NC; ++k) {
-            p.dF[f_off(p, b, t, 0, j, k)] = l1[k];
-            p.dF[f_off(p, b, t, 1, j, k)] = l2[k];
-            float s1 = 0.f, s2 = 0.f;
-            if (t > 0) {
-                s1 = __ldg(p.X + f_off(p, b, t - 1, 0, j, k));
-                s2 = __ldg(p.X + f_off(p, b, t - 1, 1, j, k));
+            for (int k = 0; k < NC; ++k) {
+                xp1[s][k] = t > 0 ? __ldg(p.X + f_off(p, b, t - 1, 0, j, k)) : 0.f;
+                xp2[s][k] = t > 0 ? __ldg(p.X + f_off(p, b, t - 1, 1, j, k)) : 0.f;
             }
-            d11 += l1[k] * s1; d12 += l1[k] * s2;
-            d21 += l2[k] * s1; d22 += l2[k] * s2;
+            if (GMS) {
+                pcw[s] = mident();  // Mc_{t-1}; identity before the first step
+                if (t > 0)
+                    pcw[s] = {__ldg(p.Mscan_in + m_off(p, b, t - 1, 0, j)),
+                              __ldg(p.Mscan_in + m_off(p, b, t - 1, 1, j)),
+                              __ldg(p.Mscan_in + m_off(p, b, t - 1, 2, j)),
+                              __ldg(p.Mscan_in + m_off(p, b, t - 1, 3, j))};
+            }
         }
-        if (GMS) {
-            Mat2 pc = mident();  // Mc_{t-1}; identity before the first step
-            if (t > 0)
-                pc = {__ldg(p.Mscan_in + m_off(p, b, t - 1, 0, j)),
-                      __ldg(p.Mscan_in + m_off(p, b, t - 1, 1, j)),
-                      __ldg(p.Mscan_in + m_off(p, b, t - 1, 2, j)),
-                      __ldg(p.Mscan_in + m_off(p, b, t - 1, 3, j))};
-            // column q of the adjoint pairs with column q of Mc_{t-1}
-            d11 += l1[NC] * pc.a + l1[NC + 1] * pc.b;
-            d12 += l1[NC] * pc.c + l1[NC + 1] * pc.d;
-            d21 += l2[NC] * pc.a + l2[NC + 1] * pc.b;
-            d22 += l2[NC] * pc.c + l2[NC + 1] * pc.d;
-        }
-        p.dM[m_off(p, b, t, 0, j)] = d11;
-        p.dM[m_off(p, b, t, 1, j)] = d12;
-        p.dM[m_off(p, b, t, 2, j)] = d21;
-        p.dM[m_off(p, b, t, 3, j)] = d22;
-        // carry M_t^T lambda_t to step t - 1
-        const Mat2 mt = mtrans(load_m(p, b, t, j));
 #pragma unroll
-        for (int k = 0; k < NV; ++k) mvec(mt, l1[k], l2[k]);
+        for (int s = 0; s < S2_W; ++s) {
+            const int64_t t = te - 1 - s;
+            if (t < t0) break;
+#pragma unroll
+            for (int k = 0; k < NV; ++k) {
+                l1[k] += g1[s][k];
+                l2[k] += g2[s][k];
+            }
+            // dF_t = lambda_t ; dM_t = sum over channels lambda_t (x) state_{t-1}
+            float d11 = 0.f, d12 = 0.f, d21 = 0.f, d22 = 0.f;
+#pragma unroll
+            for (int k = 0; k < NC; ++k) {
+                p.dF[f_off(p, b, t, 0, j, k)] = l1[k];
+                p.dF[f_off(p, b, t, 1, j, k)] = l2[k];
+                d11 += l1[k] * xp1[s][k]; d12 += l1[k] * xp2[s][k];
+                d21 += l2[k] * xp1[s][k]; d22 += l2[k] * xp2[s][k];
+            }
+            if (GMS) {
+                const Mat2& pc = pcw[s];
+                // column q of the adjoint pairs with column q of Mc_{t-1}
+                d11 += l1[NC] * pc.a + l1[NC + 1] * pc.b;
+                d12 += l1[NC] * pc.c + l1[NC + 1] * pc.d;
+                d21 += l2[NC] * pc.a + l2[NC + 1] * pc.b;
+                d22 += l2[NC] * pc.c + l2[NC + 1] * pc.d;
+            }
+            p.dM[m_off(p, b, t, 0, j)] = d11;
+            p.dM[m_off(p, b, t, 1, j)] = d12;
+            p.dM[m_off(p, b, t, 2, j)] = d21;
+            p.dM[m_off(p, b, t, 3, j)] = d22;
+            // carry M_t^T lambda_t to step t - 1
+            const Mat2 mt = mtrans(mw[s]);
+#pragma unroll
+            for (int k = 0; k < NV; ++k) mvec(mt, l1[k], l2[k]);
+        }
     }
 }
 
@@ -431,7 +482,10 @@ __device__ __forceinline__ void lin_load_window(const float* __restrict__ base, 
                                                 float2 (&u)[S2_CK]) {
     const float2* r = reinterpret_cast<const float2*>(base) + (b * q.L + ws) * q.P + j;
 #pragma unroll
-    for (int s = 0; s < S2_CK; ++s) u[s] = ws + s < t1 ? __ldg(r + s * q.P) : make_float2(0.f, 0.f);
+    for (int s = 0; s < S2_CK; ++s) {  // steps past t1 read step ws (in range) and drop it
+        const float2 v = __ldg(r + (ws + s < t1 ? s : 0) * q.P);
+        u[s] = ws + s < t1 ? v : make_float2(0.f, 0.f);
+    }
 }
 
 __global__ void __launch_bounds__(S2_NT) lin_fwd_summary(const LinParams q) {
@@ -464,8 +518,8 @@ __global__ void __launch_bounds__(S2_NT) lin_fwd_carry(const LinParams q) {
     for (int64_t c0 = 0; c0 < q.C; c0 += 8) {
         float4 sv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            sv[i] = c0 + i < q.C ? summ[(b * q.C + c0 + i) * q.P + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < 8; ++i)  // records past the end: the last one again (unused)
+            sv[i] = summ[(b * q.C + (c0 + i < q.C ? c0 + i : q.C - 1)) * q.P + j];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if (c0 + i >= q.C) break;
@@ -542,8 +596,8 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_carry(const LinParams q) {
     for (int64_t c0 = q.C - 1; c0 >= 0; c0 -= 8) {
         float4 sv[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            sv[i] = c0 - i >= 0 ? summ[(b * q.C + c0 - i) * q.P + j] : make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int i = 0; i < 8; ++i)  // records before the start: chunk 0 again (unused)
+            sv[i] = summ[(b * q.C + (c0 - i >= 0 ? c0 - i : 0)) * q.P + j];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
             if (c0 - i < 0) break;

@@ -13,6 +13,8 @@ Gradients flow to A_diag, step and Bu.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 from . import _lib
@@ -126,3 +128,70 @@ class LinossScanFn(torch.autograd.Function):
 def linoss_scan(disc: str, A_diag, step, Bu):
     """x2 of the LinOSS layer scan (complex (B, L, P)) for Bu (B, L, P) complex."""
     return LinossScanFn.apply(disc, A_diag, step, Bu)
+
+
+# ---------------------------------------------------------------------------
+# selective LinOSS scan of the Mamba-LinOSS block (fused transitions and output)
+# ---------------------------------------------------------------------------
+def _pair(re: torch.Tensor, im: torch.Tensor):
+    """fp32 (B, L, P) re/im views with unit stride along P and one shared
+    (batch, seq) stride pair (column slices of one projection keep theirs)."""
+    re, im = re.float(), im.float()
+    if re.stride(-1) != 1 or im.stride(-1) != 1 or re.stride() != im.stride():
+        re, im = re.contiguous(), im.contiguous()
+    return re, im, (ctypes.c_int64 * 2)(re.stride(0), re.stride(1))
+
+
+class LinossSelFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, disc, A_diag, s, B_re, B_im, C_re, C_im):
+        _lib.require_cuda(A_diag, s, B_re, B_im, C_re, C_im)
+        if disc not in _DISC:
+            raise ValueError(f"Discretization type {disc} not implemented")
+        lib = _lib.load()
+        Bsz, L, P = B_re.shape
+        A = A_diag.float().contiguous()
+        sv = s.float().contiguous()
+        br, bi, bst = _pair(B_re, B_im)
+        cr, ci, cst = _pair(C_re, C_im)
+        y = torch.empty((Bsz, L), device=sv.device, dtype=torch.float32)
+        work = torch.empty(lib.mmb_linoss_sel_work_floats(Bsz, L, P), device=sv.device)
+        with torch.cuda.device(sv.device):
+            st = lib.mmb_linoss_sel_fwd(_DISC[disc], Bsz, L, P, _lib.ptr(A), _lib.ptr(sv),
+                                        _lib.ptr(br), _lib.ptr(bi), bst, _lib.ptr(cr),
+                                        _lib.ptr(ci), cst, _lib.ptr(y), _lib.ptr(work),
+                                        _lib.stream_of(sv))
+        _lib.check(st, "mmb_linoss_sel_fwd")
+        ctx.save_for_backward(A, sv, br, bi, cr, ci, work)
+        ctx.disc = disc
+        ctx.dtypes = (A_diag.dtype, s.dtype, B_re.dtype, B_im.dtype, C_re.dtype, C_im.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        A, sv, br, bi, cr, ci, work = ctx.saved_tensors
+        lib = _lib.load()
+        Bsz, L, P = br.shape
+        dy = dy.float().contiguous()
+        bst = (ctypes.c_int64 * 2)(br.stride(0), br.stride(1))
+        cst = (ctypes.c_int64 * 2)(cr.stride(0), cr.stride(1))
+        dev = sv.device
+        dbr, dbi = (torch.empty((Bsz, L, P), device=dev) for _ in range(2))
+        dcr, dci = (torch.empty((Bsz, L, P), device=dev) for _ in range(2))
+        dA = torch.empty((P,), device=dev)
+        ds = torch.empty((Bsz, L), device=dev)
+        with torch.cuda.device(dev):
+            st = lib.mmb_linoss_sel_bwd(_DISC[ctx.disc], Bsz, L, P, _lib.ptr(A), _lib.ptr(sv),
+                                        _lib.ptr(br), _lib.ptr(bi), bst, _lib.ptr(cr),
+                                        _lib.ptr(ci), cst, _lib.ptr(dy), _lib.ptr(dbr),
+                                        _lib.ptr(dbi), _lib.ptr(dcr), _lib.ptr(dci), _lib.ptr(dA),
+                                        _lib.ptr(ds), _lib.ptr(work), _lib.stream_of(sv))
+        _lib.check(st, "mmb_linoss_sel_bwd")
+        grads = (dA, ds, dbr, dbi, dcr, dci)
+        return (None,) + tuple(g.to(dt) for g, dt in zip(grads, ctx.dtypes))
+
+
+def linoss_selective(disc: str, A_diag, s, B_re, B_im, C_re, C_im):
+    """y[b, t] = Re sum_p C x2 of the selective LinOSS scan (IM or IMEX) with
+    per-step step size s (B, L), A_diag (P), B and C (B, L, P) as re/im pairs."""
+    return LinossSelFn.apply(disc, A_diag, s, B_re, B_im, C_re, C_im)

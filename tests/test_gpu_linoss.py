@@ -204,3 +204,33 @@ def test_mamba_linoss_model_runs_and_matches_modes():
     y.pow(2).mean().backward()
     assert torch.isfinite(y).all()
     assert all(torch.isfinite(p.grad).all() for p in m.parameters() if p.grad is not None)
+
+
+@pytest.mark.parametrize("disc", ["IM", "IMEX"])
+@pytest.mark.parametrize("Bsz,L,P,ED", [(2, 37, 20, 6), (3, 300, 64, 8), (2, 1000, 256, 4),
+                                        (1, 8, 33, 2)])
+def test_selective_linoss_fused_vs_oracle(disc, Bsz, L, P, ED):
+    """apply_linoss_vectorized on the fused selective-LinOSS kernels (transitions
+    built per step, output contracted in-kernel) vs the fp64 restatement, with
+    B and C as column slices of one projection, as the block produces them."""
+    from momentummamba_b200.mamba_linoss import apply_linoss_vectorized
+    rng = np.random.default_rng(L + P)
+    r = 3
+    proj = rng.standard_normal((Bsz, L, r + 4 * P)) / np.sqrt(P)
+    A = np.exp(rng.uniform(-1.0, 1.0, P))
+    delta = np.log1p(np.exp(rng.standard_normal((Bsz, L, ED)) - 1.0))
+    x = rng.standard_normal((Bsz, L, ED))
+    gy = rng.standard_normal((Bsz, L, ED))
+    projt, At, dt_ = cuda(proj), cuda(A), cuda(delta)
+    parts = torch.split(projt, [r, P, P, P, P], dim=-1)
+    y = apply_linoss_vectorized(disc, At, parts[1], parts[2], parts[3], parts[4], cuda(x, False), dt_,
+                                scan_algorithm="vectorized")
+    dproj, dA, dd = torch.autograd.grad(y, [projt, At, dt_], cuda(gy, False))
+    p64, A64, d64 = (torch.from_numpy(a).double().requires_grad_() for a in (proj, A, delta))
+    q = torch.split(p64, [r, P, P, P, P], dim=-1)
+    yo = oc.mlinoss_apply(disc, A64, q[1], q[2], q[3], q[4], torch.from_numpy(x).double(), d64)
+    dpo, dAo, ddo = torch.autograd.grad(yo, [p64, A64, d64], torch.from_numpy(gy).double())
+    close(y, yo, "y")
+    close(dproj, dpo, "d(B, C)")
+    close(dA, dAo, "dA_diag")
+    close(dd, ddo, "ddelta")
