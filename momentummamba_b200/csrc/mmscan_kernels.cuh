@@ -43,6 +43,8 @@
 // pair (gstate_in).
 #pragma once
 
+#include <type_traits>
+
 #include "mmb_common.cuh"
 
 namespace mmb {
@@ -408,8 +410,8 @@ __global__ void __launch_bounds__(MM_NT)
     float bpow = 1.f;  // SUMM: beta^(steps so far)
     // checkpoint of block 0 of this thread; the next block's is ck_stride further
     const int64_t ck_stride = p.D * (2 * N);
-    float* ckw = p.ckpt ? p.ckpt + (b * ((p.L + MM_CK - 1) / MM_CK) * p.D + d) * (2 * N) + ng * 2 * NP
-                        : nullptr;
+    const bool has_ck = p.ckpt != nullptr;
+    int64_t ckoff = (b * ((p.L + MM_CK - 1) / MM_CK) * p.D + d) * (2 * N) + ng * 2 * NP;
     const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
     const float Dv = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
     const float alpha = p.alpha;
@@ -472,90 +474,104 @@ __global__ void __launch_bounds__(MM_NT)
         const float* sC = sB + Cf::TN;
         const int64_t t0 = (int64_t)c * T;
 
-        float xi[IPL], dti[IPL], dtxi[IPL];
-        prep(sx, sdl, 0, xi, dti, dtxi);
+        // The chunk's blocks.  A whole chunk (all T steps inside the sequence)
+        // runs its blocks with no branch between them, so the compiler can
+        // overlap one block's y reduction and stores with the next block's
+        // exponentials and recurrence; the last, partial chunk checks each block.
+        auto blocks = [&](auto whole_tag) {
+            constexpr bool WHOLE = decltype(whole_tag)::value;
+            float xi[IPL], dti[IPL], dtxi[IPL];
+            prep(sx, sdl, 0, xi, dti, dtxi);
 #pragma unroll
-        for (int k = 0; k < NBLK; ++k) {
-            const int64_t tb = t0 + k * MM_CK;
-            if (tb >= p.L) break;
-            if (want_end && tb + MM_CK > p.L) {
-                tail_t = tb;
+            for (int k = 0; k < NBLK; ++k) {
+                const int64_t tb = t0 + k * MM_CK;
+                if (!WHOLE) {
+                    if (tb >= p.L) break;
+                    if (want_end && tb + MM_CK > p.L) {
+                        tail_t = tb;
 #pragma unroll
-                for (int j = 0; j < NP2; ++j) {
-                    hs[j] = h[j]; vs[j] = v[j]; Ps[j] = Pp[j]; Qs[j] = Qp[j];
-                }
-                bps = bpow;
-            }
-            // broadcast the block's per-step scalars, then all its decay factors
-            float dts[MM_CK], dtxs[MM_CK];
-#pragma unroll
-            for (int s = 0; s < MM_CK; ++s) {
-                const int src = lane_base | block_owner<LB>(s - s % IPL);
-                dts[s] = __shfl_sync(FULL, dti[s % IPL], src);
-                dtxs[s] = __shfl_sync(FULL, dtxi[s % IPL], src);
-            }
-            float2 a[MM_CK][NP2];
-#pragma unroll
-            for (int s = 0; s < MM_CK; ++s) {
-#pragma unroll
-                for (int j = 0; j < NP2; ++j) {
-                    const float2 e = fmul2(f2(dts[s]), A2[j]);
-                    a[s][j] = make_float2(ex2(e.x), ex2(e.y));
-                }
-            }
-            // next block's items while the exponentials are in flight
-            float nxi[IPL], ndti[IPL], ndtxi[IPL];
-            if (k + 1 < NBLK) prep(sx, sdl, k + 1, nxi, ndti, ndtxi);
-            // checkpoint: state before the block's first step
-            if (!SUMM && ckw) {
-                if (dvalid) ckpt_store<NP>(ckw, h, v);
-                ckw += ck_stride;
-            }
-            float y[MM_CK];
-#pragma unroll
-            for (int s = 0; s < MM_CK; ++s) {
-                const int tt = k * MM_CK + s;
-                float2 bq[NP2], cq[NP2];
-                ld_pairs<NP>(sB + tt * N + ng * NP, bq);
-                if (!SUMM) ld_pairs<NP>(sC + tt * N + ng * NP, cq);
-#pragma unroll
-                for (int j = 0; j < NP2; ++j) {
-                    v[j] = ffma2(beta2, v[j], fmul2(f2(dtxs[s]), bq[j]));
-                    h[j] = ffma2(a[s][j], h[j], v[j]);
-                    if (SUMM) {
-                        Pp[j] = fmul2(a[s][j], Pp[j]);
-                        Qp[j] = ffma2(a[s][j], Qp[j], f2(bpow));
+                        for (int j = 0; j < NP2; ++j) {
+                            hs[j] = h[j]; vs[j] = v[j]; Ps[j] = Pp[j]; Qs[j] = Qp[j];
+                        }
+                        bps = bpow;
                     }
                 }
-                if (SUMM)
-                    bpow *= p.beta;
-                else
-                    y[s] = dot_pairs(cq, h);
-            }
-            if (!SUMM) {
-                reduce_scatter<MM_CK, 0, Cf::LOG2G>(y, lane);
-                // finish this lane's items: D skip, gate, store
+                // broadcast the block's per-step scalars, then all its decay factors
+                float dts[MM_CK], dtxs[MM_CK];
 #pragma unroll
-                for (int i = 0; i < IPL; ++i) {
-                    const int tt = k * MM_CK + ibase + i;
-                    const int64_t gt = t0 + tt;
-                    float o = fmaf(Dv, xi[i], y[i]);
-                    if (HAS_Z) {
-                        const float zv = sz[Cf::dix(tt, dl)];
-                        o *= zv * sigmoid_f(zv);
+                for (int s = 0; s < MM_CK; ++s) {
+                    const int src = lane_base | block_owner<LB>(s - s % IPL);
+                    dts[s] = __shfl_sync(FULL, dti[s % IPL], src);
+                    dtxs[s] = __shfl_sync(FULL, dtxi[s % IPL], src);
+                }
+                float2 a[MM_CK][NP2];
+#pragma unroll
+                for (int s = 0; s < MM_CK; ++s) {
+#pragma unroll
+                    for (int j = 0; j < NP2; ++j) {
+                        const float2 e = fmul2(f2(dts[s]), A2[j]);
+                        a[s][j] = make_float2(ex2(e.x), ex2(e.y));
                     }
-                    if (item_lane && dvalid && gt < p.L) E::store(gout, (b * p.L + gt) * p.D + d, o);
                 }
-            }
-            if (k + 1 < NBLK) {
+                // next block's items while the exponentials are in flight
+                float nxi[IPL], ndti[IPL], ndtxi[IPL];
+                if (k + 1 < NBLK) prep(sx, sdl, k + 1, nxi, ndti, ndtxi);
+                // checkpoint: state before the block's first step
+                if (!SUMM) {
+                    if (has_ck && dvalid) ckpt_store<NP>(p.ckpt + ckoff, h, v);
+                    ckoff += ck_stride;
+                }
+                float y[MM_CK];
 #pragma unroll
-                for (int i = 0; i < IPL; ++i) {
-                    xi[i] = nxi[i];
-                    dti[i] = ndti[i];
-                    dtxi[i] = ndtxi[i];
+                for (int s = 0; s < MM_CK; ++s) {
+                    const int tt = k * MM_CK + s;
+                    float2 bq[NP2], cq[NP2];
+                    ld_pairs<NP>(sB + tt * N + ng * NP, bq);
+                    if (!SUMM) ld_pairs<NP>(sC + tt * N + ng * NP, cq);
+#pragma unroll
+                    for (int j = 0; j < NP2; ++j) {
+                        v[j] = ffma2(beta2, v[j], fmul2(f2(dtxs[s]), bq[j]));
+                        h[j] = ffma2(a[s][j], h[j], v[j]);
+                        if (SUMM) {
+                            Pp[j] = fmul2(a[s][j], Pp[j]);
+                            Qp[j] = ffma2(a[s][j], Qp[j], f2(bpow));
+                        }
+                    }
+                    if (SUMM)
+                        bpow *= p.beta;
+                    else
+                        y[s] = dot_pairs(cq, h);
+                }
+                if (!SUMM) {
+                    reduce_scatter<MM_CK, 0, Cf::LOG2G>(y, lane);
+                    // finish this lane's items: D skip, gate, store
+#pragma unroll
+                    for (int i = 0; i < IPL; ++i) {
+                        const int tt = k * MM_CK + ibase + i;
+                        const int64_t gt = t0 + tt;
+                        float o = fmaf(Dv, xi[i], y[i]);
+                        if (HAS_Z) {
+                            const float zv = sz[Cf::dix(tt, dl)];
+                            o *= zv * sigmoid_f(zv);
+                        }
+                        if (item_lane && dvalid && (WHOLE || gt < p.L))
+                            E::store(gout, (b * p.L + gt) * p.D + d, o);
+                    }
+                }
+                if (k + 1 < NBLK) {
+#pragma unroll
+                    for (int i = 0; i < IPL; ++i) {
+                        xi[i] = nxi[i];
+                        dti[i] = ndti[i];
+                        dtxi[i] = ndtxi[i];
+                    }
                 }
             }
-        }
+        };
+        if (t0 + T <= p.L)
+            blocks(std::true_type{});
+        else
+            blocks(std::false_type{});
         if (c + 1 < nchunks) __syncthreads();
     }
 
