@@ -505,29 +505,92 @@ __global__ void __launch_bounds__(S2_NT) lin_fwd_summary(const LinParams q) {
     reinterpret_cast<float4*>(lin_summ(q))[idx] = make_float4(x1r, x1i, x2r, x2i);
 }
 
+// ---------------------------------------------------------------------------
+// Chunk carries of the LinOSS layer.  The transition is the same every step,
+// so across chunks the carry follows x_{c+1} = K x_c + w_c with one constant K
+// (a power of M); a warp takes 32 consecutive chunks of a chain and scans them
+// with shuffles (Hillis-Steele, weights K^(2^k)), instead of one thread walking
+// every chunk of its chain.
+// ---------------------------------------------------------------------------
+struct Cv2 {  // complex 2-vector (x1, x2)
+    float x1r, x1i, x2r, x2i;
+};
+__device__ __forceinline__ void cv_mul(const Mat2& m, Cv2& v) {
+    mvec(m, v.x1r, v.x2r);
+    mvec(m, v.x1i, v.x2i);
+}
+__device__ __forceinline__ Cv2 cv_add(const Cv2& a, const Cv2& b) {
+    return {a.x1r + b.x1r, a.x1i + b.x1i, a.x2r + b.x2r, a.x2i + b.x2i};
+}
+__device__ __forceinline__ Cv2 cv_shfl_up(const Cv2& v, int d) {
+    return {__shfl_up_sync(0xffffffffu, v.x1r, d), __shfl_up_sync(0xffffffffu, v.x1i, d),
+            __shfl_up_sync(0xffffffffu, v.x2r, d), __shfl_up_sync(0xffffffffu, v.x2i, d)};
+}
+__device__ __forceinline__ Cv2 cv_shfl(const Cv2& v, int src) {
+    return {__shfl_sync(0xffffffffu, v.x1r, src), __shfl_sync(0xffffffffu, v.x1i, src),
+            __shfl_sync(0xffffffffu, v.x2r, src), __shfl_sync(0xffffffffu, v.x2i, src)};
+}
+__device__ __forceinline__ Mat2 mpow(Mat2 m, int64_t e) {
+    Mat2 r = mident();
+    while (e > 0) {
+        if (e & 1) r = mmul(m, r);
+        m = mmul(m, m);
+        e >>= 1;
+    }
+    return r;
+}
+
+// Exclusive scan over the warp's lanes of x_{l+1} = K x_l + w_l from x_0 = xin,
+// with Kp[k] = K^(2^k) (k = 0..5) and Kl = K^lane: lane l receives x_l in
+// `excl`; every lane gets x_32 back.
+__device__ __forceinline__ Cv2 warp_carry_scan(const Mat2 (&Kp)[6], const Mat2& Kl, Cv2 w,
+                                               const Cv2& xin, int lane, Cv2& excl) {
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {  // w_l <- sum_{i <= l} K^(l - i) w_i
+        Cv2 o = cv_shfl_up(w, 1 << k);
+        cv_mul(Kp[k], o);
+        if (lane >= (1 << k)) w = cv_add(w, o);
+    }
+    const Cv2 prev = cv_shfl_up(w, 1);
+    Cv2 kx = xin;
+    cv_mul(Kl, kx);
+    excl = lane ? cv_add(kx, prev) : kx;
+    Cv2 k32 = xin;
+    cv_mul(Kp[5], k32);
+    return cv_add(k32, cv_shfl(w, 31));
+}
+
+__device__ __forceinline__ void carry_powers(const Mat2& K, int lane, Mat2 (&Kp)[6], Mat2& Kl) {
+    Kp[0] = K;
+#pragma unroll
+    for (int k = 1; k < 6; ++k) Kp[k] = mmul(Kp[k - 1], Kp[k - 1]);
+    Kl = mident();
+#pragma unroll
+    for (int k = 0; k < 5; ++k)
+        if ((lane >> k) & 1) Kl = mmul(Kp[k], Kl);
+}
+
+// forward: x entering chunk c, x_{c+1} = M^T x_c + summ_c (T steps per chunk)
 __global__ void __launch_bounds__(S2_NT) lin_fwd_carry(const LinParams q) {
-    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
-    if (idx >= q.Bsz * q.P) return;
-    const int64_t j = idx % q.P, b = idx / q.P;
-    const LinCoef k = lin_coef(q.disc, q.A[j], q.step[j]);
-    Mat2 mT = mident();  // M^T, the transition over a full chunk
-    for (int64_t s = 0; s < q.T; ++s) mT = mmul(k.m, mT);
-    float x1r = 0.f, x1i = 0.f, x2r = 0.f, x2i = 0.f;
+    const int64_t chain = (int64_t)blockIdx.x * (S2_NT / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (chain >= q.Bsz * q.P) return;  // whole warps
+    const int64_t j = chain % q.P, b = chain / q.P;
+    Mat2 Kp[6], Kl;
+    carry_powers(mpow(lin_coef(q.disc, q.A[j], q.step[j]).m, q.T), lane, Kp, Kl);
     const float4* __restrict__ summ = reinterpret_cast<const float4*>(lin_summ(q));
     float4* __restrict__ carry = reinterpret_cast<float4*>(lin_carry(q));
-    for (int64_t c0 = 0; c0 < q.C; c0 += 8) {
-        float4 sv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)  // records past the end: the last one again (unused)
-            sv[i] = summ[(b * q.C + (c0 + i < q.C ? c0 + i : q.C - 1)) * q.P + j];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (c0 + i >= q.C) break;
-            carry[(b * q.C + c0 + i) * q.P + j] = make_float4(x1r, x1i, x2r, x2i);
-            mvec(mT, x1r, x2r);
-            mvec(mT, x1i, x2i);
-            x1r += sv[i].x; x1i += sv[i].y; x2r += sv[i].z; x2i += sv[i].w;
+    Cv2 x = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t c0 = 0; c0 < q.C; c0 += 32) {
+        const int64_t c = c0 + lane;
+        Cv2 w = {0.f, 0.f, 0.f, 0.f};
+        if (c < q.C) {
+            const float4 sv = summ[(b * q.C + c) * q.P + j];
+            w = {sv.x, sv.y, sv.z, sv.w};
         }
+        Cv2 ex;
+        x = warp_carry_scan(Kp, Kl, w, x, lane, ex);
+        if (c < q.C) carry[(b * q.C + c) * q.P + j] = make_float4(ex.x1r, ex.x1i, ex.x2r, ex.x2i);
     }
 }
 
@@ -581,33 +644,32 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_summary(const LinParams q) {
     reinterpret_cast<float4*>(lin_summ(q))[idx] = make_float4(l1r, l1i, l2r, l2i);
 }
 
+// backward: mu_c = M^T lambda at the first step of chunk c + 1 (zero for the
+// last chunk, the only one that may be shorter than T); lambda at chunk c's
+// first step is lam_loc_c + (M^T)^(T-1) mu_c, so taking chunks from the last,
+// mu_{c-1} = (M^T)^T mu_c + M^T lam_loc_c.
 __global__ void __launch_bounds__(S2_NT) lin_bwd_carry(const LinParams q) {
-    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
-    if (idx >= q.Bsz * q.P) return;
-    const int64_t j = idx % q.P, b = idx / q.P;
+    const int64_t chain = (int64_t)blockIdx.x * (S2_NT / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (chain >= q.Bsz * q.P) return;  // whole warps
+    const int64_t j = chain % q.P, b = chain / q.P;
     const Mat2 mt = mtrans(lin_coef(q.disc, q.A[j], q.step[j]).m);
-    // mu_c = M^T lambda_{first step of chunk c+1}; lambda_{t0} = lam_loc + (M^T)^(T-1) mu_c.
-    // Only the last chunk can be shorter than T, and its mu is zero.
-    Mat2 pw = mident();
-    for (int64_t s = 1; s < q.T; ++s) pw = mmul(mt, pw);
-    float m1r = 0.f, m1i = 0.f, m2r = 0.f, m2i = 0.f;
+    Mat2 Kp[6], Kl;
+    carry_powers(mpow(mt, q.T), lane, Kp, Kl);
     const float4* __restrict__ summ = reinterpret_cast<const float4*>(lin_summ(q));
     float4* __restrict__ carry = reinterpret_cast<float4*>(lin_carry(q));
-    for (int64_t c0 = q.C - 1; c0 >= 0; c0 -= 8) {
-        float4 sv[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)  // records before the start: chunk 0 again (unused)
-            sv[i] = summ[(b * q.C + (c0 - i >= 0 ? c0 - i : 0)) * q.P + j];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            if (c0 - i < 0) break;
-            carry[(b * q.C + c0 - i) * q.P + j] = make_float4(m1r, m1i, m2r, m2i);
-            mvec(pw, m1r, m2r);
-            mvec(pw, m1i, m2i);
-            m1r += sv[i].x; m1i += sv[i].y; m2r += sv[i].z; m2i += sv[i].w;
-            mvec(mt, m1r, m2r);
-            mvec(mt, m1i, m2i);
+    Cv2 m = {0.f, 0.f, 0.f, 0.f};
+    for (int64_t r0 = 0; r0 < q.C; r0 += 32) {
+        const int64_t c = q.C - 1 - (r0 + lane);  // lanes take chunks from the last
+        Cv2 w = {0.f, 0.f, 0.f, 0.f};
+        if (c >= 0) {
+            const float4 sv = summ[(b * q.C + c) * q.P + j];
+            w = {sv.x, sv.y, sv.z, sv.w};
+            cv_mul(mt, w);
         }
+        Cv2 ex;
+        m = warp_carry_scan(Kp, Kl, w, m, lane, ex);
+        if (c >= 0) carry[(b * q.C + c) * q.P + j] = make_float4(ex.x1r, ex.x1i, ex.x2r, ex.x2i);
     }
 }
 
@@ -803,7 +865,7 @@ extern "C" int mmb_linoss_fwd(int32_t disc, int64_t batch, int64_t L, int64_t P,
     q.disc = disc; q.A = A_diag; q.step = step; q.Bu = Bu; q.x2 = x2; q.work = work;
     cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
     lin_fwd_summary<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
-    lin_fwd_carry<<<s2_blocks(q.Bsz * q.P), S2_NT, 0, st>>>(q);
+    lin_fwd_carry<<<s2_blocks(q.Bsz * q.P * 32), S2_NT, 0, st>>>(q);
     lin_fwd_final<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
     return mmb_launch_status();
 }
@@ -827,7 +889,7 @@ extern "C" int mmb_linoss_bwd(int32_t disc, int64_t batch, int64_t L, int64_t P,
                         sizeof(float) * q.P * 8, st) != cudaSuccess)
         return MMB_ERR_LAUNCH;
     lin_bwd_summary<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
-    lin_bwd_carry<<<s2_blocks(q.Bsz * q.P), S2_NT, 0, st>>>(q);
+    lin_bwd_carry<<<s2_blocks(q.Bsz * q.P * 32), S2_NT, 0, st>>>(q);
     lin_bwd_final<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
     lin_bwd_params<<<(unsigned)((P + 127) / 128), 128, 0, st>>>(q);
     return mmb_launch_status();
