@@ -68,9 +68,9 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
-def load_traffic():
-    """DRAM bytes per backward launch from the committed ncu capture, if any."""
-    path = os.path.join(ROOT, "profiles", "mmscan_bwd_traffic.json")
+def load_traffic(name="mmscan_bwd_traffic.json"):
+    """DRAM bytes per backward launch (or call) from the committed ncu capture, if any."""
+    path = os.path.join(ROOT, "profiles", name)
     try:
         with open(path) as f:
             return json.load(f)
@@ -784,6 +784,7 @@ def run_linoss(args):
     bwd_b = elems * 24 + 4 * P * 4          # read Bu, dx2; write dBu
     peak, peak_kind = load_peaks()
     achieved = bwd_b / (t["bwd_IM"] / 1e3) / 1e9
+    tr = load_traffic("linoss_bwd_traffic.json")
     return {
         "metric": METRIC, "value": job_rate(2 * elems * args.steps, world, ms), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -793,10 +794,12 @@ def run_linoss(args):
                                "complex Bu ~ N(0,1), A ~ U[0,1], step = exp(U[ln 1e-3, ln 1e-1]); "
                                "elements = B*L*P oscillator steps per discretisation",
                    "parallelism": f"batch-sharded x{world}", "launch": "cuda graph",
-                   "l2": "inputs larger than L2 (Bu, dx2 268 MB each)"},
-        "roofline": {"kernel": "lin_bwd (IM)", "bound": "hbm", "achieved": achieved, "peak": peak,
+                   "l2": "inputs larger than L2 (Bu, dx2 134 MB each; 1.3 GB of algorithmic traffic per step)"},
+        "roofline": {"kernel": "lin_bwd (IM): summary + carry + final + params launches",
+                     "bound": "hbm", "achieved": achieved, "peak": peak,
                      "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": achieved / peak,
-                     "algorithmic_bytes": bwd_b, "ms_per_launch": t["bwd_IM"], "traffic": None},
+                     "algorithmic_bytes": bwd_b, "ms_per_launch": t["bwd_IM"],
+                     "traffic": tr["dram_bytes_per_call"] if tr else None},
         "kernels": {k: {"ms": v, "algorithmic_bytes": fwd_b if k.startswith("fwd") else bwd_b,
                         "GB/s": (fwd_b if k.startswith("fwd") else bwd_b) / (v / 1e3) / 1e9}
                     for k, v in t.items()},
