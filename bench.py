@@ -357,12 +357,15 @@ def run_b200(args):
     return line
 
 
-def run_e2e(torch, fn, dev, layers, args, steps=3):
+def run_e2e(torch, fn, dev, layers, args, steps=8):
     """Same metric through selective_scan_momentum_fn + autograd, with each
     layer's inputs copied in from pinned host memory and all its outputs copied
     back every step.  The copies run on two side streams so that the next
     layer's inputs come in while the previous layer's outputs go out (PCIe is
-    full duplex); the scans run on the current stream in layer order."""
+    full duplex), and a step's uploads may start while the previous step's
+    outputs still go out (steady state of a stream of batches); the scans run on
+    the current stream in layer order.  The timed region ends after the last
+    step's outputs reached the host."""
     host_in, host_out = [], []
     for ly in layers:
         host_in.append({k: getattr(ly, k).cpu().pin_memory()
@@ -378,7 +381,6 @@ def run_e2e(torch, fn, dev, layers, args, steps=3):
 
     def one():
         dev_in = [None] * LAYERS
-        s_in.wait_stream(comp)  # the step's copies start after the previous step
 
         def fetch(i):
             with torch.cuda.stream(s_in):
@@ -412,23 +414,25 @@ def run_e2e(torch, fn, dev, layers, args, steps=3):
                     v = v.detach()
                     v.record_stream(s_out)
                     host_out[i][k].copy_(v, non_blocking=True)
-        comp.wait_stream(s_out)
 
     one()
     torch.cuda.synchronize()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(comp)
+    s_in.wait_stream(comp)
+    s_out.wait_stream(comp)
     for _ in range(steps):
         one()
+    comp.wait_stream(s_out)
     e1.record(comp)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
     return {"value": ELEMS_PER_LAYER * LAYERS / (ms / 1e3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
             "steps": steps, "api": "selective_scan_momentum_fn + torch.autograd.grad",
-            "copies": "pinned host buffers; inputs of layer i+1 in while outputs of layer i "
-                      "go out (two copy streams)"}
+            "copies": "pinned host buffers; inputs of layer i+1 (and of the next step) in "
+                      "while outputs of layer i go out (two copy streams)"}
 
 
 # ---------------------------------------------------------------------------
