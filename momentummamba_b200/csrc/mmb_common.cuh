@@ -28,6 +28,13 @@ __device__ __forceinline__ void cp_async16(void* sdst, const void* gsrc, bool va
                  : "memory");
 }
 
+__device__ __forceinline__ void cp_async8(void* sdst, const void* gsrc, bool valid) {
+    const int n = valid ? 8 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;\n" ::"r"(smem_u32(sdst)),
+                 "l"(gsrc), "r"(n)
+                 : "memory");
+}
+
 __device__ __forceinline__ void cp_async4(void* sdst, const void* gsrc, bool valid) {
     const int n = valid ? 4 : 0;
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(smem_u32(sdst)),

@@ -495,12 +495,16 @@ __global__ void __launch_bounds__(S2_NT) lin_fwd_summary(const LinParams q) {
     const int64_t t0 = c * q.T, t1 = min64(q.L, t0 + q.T);
     const LinCoef k = lin_coef(q.disc, q.A[j], q.step[j]);
     float x1r = 0.f, x1i = 0.f, x2r = 0.f, x2i = 0.f;
+    // the next window's loads are issued before this window's recurrence
+    float2 u[S2_CK], un[S2_CK];
+    lin_load_window(q.Bu, q, b, t0, t1, j, u);
     for (int64_t ws = t0; ws < t1; ws += S2_CK) {
-        float2 u[S2_CK];
-        lin_load_window(q.Bu, q, b, ws, t1, j, u);
+        if (ws + S2_CK < t1) lin_load_window(q.Bu, q, b, ws + S2_CK, t1, j, un);
 #pragma unroll
         for (int s = 0; s < S2_CK; ++s)
             if (ws + s < t1) lin_step(k, u[s], x1r, x1i, x2r, x2i);
+#pragma unroll
+        for (int s = 0; s < S2_CK; ++s) u[s] = un[s];
     }
     reinterpret_cast<float4*>(lin_summ(q))[idx] = make_float4(x1r, x1i, x2r, x2i);
 }
@@ -626,9 +630,12 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_summary(const LinParams q) {
     const Mat2 mt = mtrans(lin_coef(q.disc, q.A[j], q.step[j]).m);
     float l1r = 0.f, l1i = 0.f, l2r = 0.f, l2i = 0.f;
     bool first = true;
-    for (int64_t ws = t0 + (t1 - 1 - t0) / S2_CK * S2_CK; ws >= t0; ws -= S2_CK) {
-        float2 g[S2_CK];
-        lin_load_window(q.dx2, q, b, ws, t1, j, g);
+    // the next (earlier) window's loads are issued before this window's recurrence
+    const int64_t wlast = t0 + (t1 - 1 - t0) / S2_CK * S2_CK;
+    float2 g[S2_CK], gn[S2_CK];
+    lin_load_window(q.dx2, q, b, wlast, t1, j, g);
+    for (int64_t ws = wlast; ws >= t0; ws -= S2_CK) {
+        if (ws - S2_CK >= t0) lin_load_window(q.dx2, q, b, ws - S2_CK, t1, j, gn);
 #pragma unroll
         for (int s = S2_CK - 1; s >= 0; --s) {
             if (ws + s >= t1) continue;
@@ -640,6 +647,8 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_summary(const LinParams q) {
             l2r += g[s].x;
             l2i += g[s].y;
         }
+#pragma unroll
+        for (int s = 0; s < S2_CK; ++s) g[s] = gn[s];
     }
     reinterpret_cast<float4*>(lin_summ(q))[idx] = make_float4(l1r, l1i, l2r, l2i);
 }
@@ -676,8 +685,16 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_carry(const LinParams q) {
 // Per chunk, 8-step windows in reverse: rebuild x_{t-1} from the forward
 // checkpoint, then run the adjoint; dBu_t = f1 lambda1_t + f2 lambda2_t;
 // dM += lambda_t x_{t-1}^T and (df1, df2) += (lambda1, lambda2) . Bu_t.
-__global__ void __launch_bounds__(S2_NT) lin_bwd_final(const LinParams q) {
-    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
+// Each thread copies its next window (Bu, dx2, checkpoint) into its own slots
+// of shared memory with cp.async while it computes the current one, so a
+// window's loads are in flight during the previous window's recurrences (a
+// thread reads back only what it copied: no block barrier).
+constexpr int LIN_BWD_SLOT = 2 * S2_CK * 2 + 4;  // floats per thread and buffer: Bu, dx2, ckpt
+constexpr size_t LIN_BWD_SMEM = sizeof(float) * 2 * LIN_BWD_SLOT * S2_NT;
+__global__ void __launch_bounds__(S2_NT, 2) lin_bwd_final(const LinParams q) {
+    extern __shared__ float4 lin_sm4[];
+    const int tid = threadIdx.x;
+    const int64_t idx = (int64_t)blockIdx.x * S2_NT + tid;
     const bool active = idx < q.Bsz * q.C * q.P;
     float g[6] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     int64_t j = 0;
@@ -691,12 +708,43 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_final(const LinParams q) {
         float l1r = mu.x, l1i = mu.y, l2r = mu.z, l2i = mu.w;  // M^T lambda_{t+1}
         const float4* __restrict__ ck = reinterpret_cast<const float4*>(lin_ckpt(q));
         float2* __restrict__ dbu = reinterpret_cast<float2*>(q.dBu) + b * q.L * q.P + j;
+        const float2* __restrict__ bu = reinterpret_cast<const float2*>(q.Bu) + b * q.L * q.P + j;
+        const float2* __restrict__ gx = reinterpret_cast<const float2*>(q.dx2) + b * q.L * q.P + j;
+        // shared slots: [buffer][Bu(8) | dx2(8) | ckpt] float2/float4 units, thread-minor
+        float2* sm2 = reinterpret_cast<float2*>(lin_sm4);
+        float4* smck = lin_sm4 + 2 * 2 * S2_CK * S2_NT / 2;
+        auto slot2 = [&](int buf, int arr, int s) -> float2* {
+            return sm2 + ((buf * 2 + arr) * S2_CK + s) * S2_NT + tid;
+        };
+        // copy window [ws, ws + 8) (steps past t1 read step ws and are dropped)
+        auto issue = [&](int buf, int64_t ws) {
+#pragma unroll
+            for (int s = 0; s < S2_CK; ++s) {
+                const int64_t t = ws + s < t1 ? ws + s : ws;
+                cp_async8(slot2(buf, 0, s), bu + t * q.P, true);
+                cp_async8(slot2(buf, 1, s), gx + t * q.P, true);
+            }
+            cp_async16(smck + buf * S2_NT + tid, ck + (b * q.K + ws / S2_CK) * q.P + j, true);
+            cp_async_commit();
+        };
         // windows [ws, ws + 8) of the chunk (t0 and T are multiples of 8)
-        for (int64_t ws = t0 + (t1 - 1 - t0) / S2_CK * S2_CK; ws >= t0; ws -= S2_CK) {
+        int64_t ws = t0 + (t1 - 1 - t0) / S2_CK * S2_CK;
+        int buf = 0;
+        issue(0, ws);
+        for (; ws >= t0; ws -= S2_CK, buf ^= 1) {
+            if (ws - S2_CK >= t0)
+                issue(buf ^ 1, ws - S2_CK);
+            else
+                cp_async_commit();  // an empty group keeps the wait count uniform
+            cp_async_wait<1>();
             float2 us[S2_CK], gs[S2_CK];
-            lin_load_window(q.Bu, q, b, ws, t1, j, us);
-            lin_load_window(q.dx2, q, b, ws, t1, j, gs);
-            const float4 x0 = ck[(b * q.K + ws / S2_CK) * q.P + j];
+#pragma unroll
+            for (int s = 0; s < S2_CK; ++s) {
+                const bool in = ws + s < t1;
+                us[s] = in ? *slot2(buf, 0, s) : make_float2(0.f, 0.f);
+                gs[s] = in ? *slot2(buf, 1, s) : make_float2(0.f, 0.f);
+            }
+            const float4 x0 = smck[buf * S2_NT + tid];
             float xs[S2_CK + 1][4];
             xs[0][0] = x0.x; xs[0][1] = x0.y; xs[0][2] = x0.z; xs[0][3] = x0.w;
 #pragma unroll
@@ -722,6 +770,7 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_final(const LinParams q) {
                 mvec(mt, l1i, l2i);
             }
         }
+        cp_async_wait<0>();
     }
     // sum over (b, chunk) into per-oscillator accumulators; a warp spans
     // consecutive p, so each thread adds its own
@@ -890,7 +939,10 @@ extern "C" int mmb_linoss_bwd(int32_t disc, int64_t batch, int64_t L, int64_t P,
         return MMB_ERR_LAUNCH;
     lin_bwd_summary<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
     lin_bwd_carry<<<s2_blocks(q.Bsz * q.P * 32), S2_NT, 0, st>>>(q);
-    lin_bwd_final<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, 0, st>>>(q);
+    static int attr_done[MMB_MAX_DEVICES] = {};
+    const int sa = mmb_smem_attr(lin_bwd_final, LIN_BWD_SMEM, attr_done);
+    if (sa != MMB_OK) return sa;
+    lin_bwd_final<<<s2_blocks(q.Bsz * q.C * q.P), S2_NT, LIN_BWD_SMEM, st>>>(q);
     lin_bwd_params<<<(unsigned)((P + 127) / 128), 128, 0, st>>>(q);
     return mmb_launch_status();
 }
