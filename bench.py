@@ -350,7 +350,7 @@ def run_b200(args):
         },
         "hbm_gbs_step": LAYERS * (fwd_b + bwd_b) * args.steps / (ms / 1e3) / 1e9,
         "e2e": e2e,
-        "gpu_launches": 2 * LAYERS * args.steps,
+        "gpu_launches": 3 * LAYERS * args.steps,  # per layer: forward, clearing of the sums, backward
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
@@ -672,8 +672,9 @@ def run_long(args):
                      "algorithmic_bytes_per_gpu_step": fb + bb, "traffic": None,
                      "scope": "whole step per GPU (fwd+bwd kernels, carries, collectives)"},
         "phases_ms": phases,
-        # rank 0: forward, backward; with segments also both summaries and the adjoint fold
-        "gpu_launches": (2 if world == 1 else 5) * args.steps,
+        # rank 0: forward, clearing of the backward's sums, backward; with segments also
+        # both summaries and the adjoint fold
+        "gpu_launches": (3 if world == 1 else 6) * args.steps,
         "clocks": clocks,
     }
 

@@ -83,6 +83,26 @@ static int forward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t, cud
     return launch(desc, p, MM_FWD, s);
 }
 
+// Zeroing of the backward's atomic sums.  dB and dC (16-byte aligned, length a
+// multiple of 4) take float4 stores; dA, dD and d(delta_bias) scalar ones.
+struct ZeroList {
+    float* p[5];
+    int64_t n[5];
+};
+__global__ void zero_sums_kernel(const ZeroList z) {
+    const int64_t i0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    const int64_t step = (int64_t)gridDim.x * blockDim.x;
+    for (int k = 0; k < 5; ++k) {
+        if (!z.p[k]) continue;
+        if (k < 2) {
+            float4* q = reinterpret_cast<float4*>(z.p[k]);
+            for (int64_t e = i0; e < z.n[k] / 4; e += step) q[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        } else {
+            for (int64_t e = i0; e < z.n[k]; e += step) z.p[k][e] = 0.f;
+        }
+    }
+}
+
 static int backward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t, cudaStream_t s) {
     if (!t) return MMB_ERR_NULL;
     MMParams p;
@@ -108,17 +128,21 @@ static int backward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t, cu
     const int64_t N = desc->dstate;
     const size_t bln = (size_t)(p.Bsz * p.L * N) * sizeof(float);
     const size_t dsz = (size_t)p.D * sizeof(float);
-    // the sums are accumulated with atomics: clear them on the stream first
+    // the sums are accumulated with atomics: clear them on the stream first,
+    // all five in one launch
+    ZeroList zl{};
     float* const sums[5] = {p.dB, p.dC, p.dA, p.dD, p.ddbias};
     const size_t bytes[5] = {bln, bln, (size_t)N * dsz, dsz, dsz};
+    int64_t total = 0;
     for (int i = 0; i < 5; ++i) {
-        if (!sums[i]) continue;
-        const cudaError_t e = cudaMemsetAsync(sums[i], 0, bytes[i], s);
-        if (e != cudaSuccess) {
-            mmb_record_cuda_error(e);
-            return MMB_ERR_LAUNCH;
-        }
+        zl.p[i] = sums[i];
+        zl.n[i] = sums[i] ? (int64_t)(bytes[i] / sizeof(float)) : 0;
+        total += zl.n[i];
     }
+    const int64_t blocks = min64((total / 4 + 255) / 256 + 1, 148 * 4);
+    zero_sums_kernel<<<(unsigned)blocks, 256, 0, s>>>(zl);
+    const int zst = mmb_launch_status();
+    if (zst != MMB_OK) return zst;
     return launch(desc, p, MM_BWD, s);
 }
 
