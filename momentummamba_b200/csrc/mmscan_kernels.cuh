@@ -59,14 +59,15 @@ constexpr int MM_NS = 2;
 
 __host__ __device__ constexpr int ilog2c(int v) { return v <= 1 ? 0 : 1 + ilog2c(v / 2); }
 
-template <int N, int NP>
+template <int N, int NP, int NT = MM_NT>
 struct MMCfg {
+    static constexpr int NTH = NT;                    // threads per CTA
     static constexpr int NP2 = NP / 2;                // packed pairs per thread
     static constexpr int G = N / NP;                  // lanes per channel
     static constexpr int LOG2G = ilog2c(G);
     static constexpr int LB = LOG2G < 3 ? LOG2G : 3;  // lane bits that split an 8-step block
     static constexpr int IPL = MM_CK >> LB;           // (t, d) items a lane owns per block
-    static constexpr int DT = MM_NT / G;              // channels per CTA
+    static constexpr int DT = NT / G;                 // channels per CTA
     static constexpr int DPW = 32 / G;                // channels per warp
     static constexpr int LOG2DPW = 5 - LOG2G;
     // (T x DT) fp32 activation tile: dense rows of DT floats whose 16-byte
@@ -80,7 +81,8 @@ struct MMCfg {
         return (r * DT + c) ^ (((r * DT + c) >> 3) & SWM);
     }
     static constexpr int TN = MM_T * N;
-    static_assert((NP == 2 || NP == 4) && N % NP == 0 && G >= 2 && G <= 16, "unsupported shape");
+    static_assert((NP == 2 || NP == 4) && N % NP == 0 && G >= 2 && G <= 16 && DT >= 4,
+                  "unsupported shape");
 };
 
 // Shared-memory layout of one kernel: NDT (T x DT) activation tiles and two
@@ -90,9 +92,9 @@ struct MMCfg {
 // kernel widens.  Stages start on 1024-byte boundaries (the swizzle period);
 // MM_SMEM_ALIGN bytes of slack let the kernel align its dynamic base.
 constexpr int MM_SMEM_ALIGN = 1024;
-template <int N, int NP, int NDT, int EBYTES>
+template <int N, int NP, int NDT, int EBYTES, int NT = MM_NT>
 struct MMSmem {
-    using Cf = MMCfg<N, NP>;
+    using Cf = MMCfg<N, NP, NT>;
     static constexpr bool WIDE = EBYTES == 2;
     static constexpr int F32 = NDT * Cf::TR + 2 * Cf::TN;             // floats per fp32 stage
     static constexpr int RAW = NDT * MM_T * Cf::DT + 2 * MM_T * N;    // 16-bit words per raw stage
@@ -259,10 +261,10 @@ __device__ __forceinline__ void ckpt_load(const float* src, float2 (&h)[NP / 2],
 // the tiles it is about to copy and issues one tensor copy per tile; the other
 // threads only wait on the barrier.  Otherwise every thread issues cp.async
 // copies and waits on its own groups.
-template <int N, int NP, int NDT, class E>
+template <int N, int NP, int NDT, class E, int NT = MM_NT>
 struct MMStager {
-    using Cf = MMCfg<N, NP>;
-    using Sm = MMSmem<N, NP, NDT, E::BYTES>;
+    using Cf = MMCfg<N, NP, NT>;
+    using Sm = MMSmem<N, NP, NDT, E::BYTES, NT>;
     using ET = typename E::T;
     float* smem;      // aligned dynamic base
     uint64_t* bars;   // MM_NS transaction barriers
@@ -292,11 +294,11 @@ struct MMStager {
             return;
         }
         if constexpr (Sm::WIDE)
-            stage_tile_b16<MM_T, Cf::DT, Cf::DT, MM_NT>(static_cast<uint16_t*>(dtile(slot, i)),
+            stage_tile_b16<MM_T, Cf::DT, Cf::DT, NT>(static_cast<uint16_t*>(dtile(slot, i)),
                                                         reinterpret_cast<const uint16_t*>(g),
                                                         gstride, rows, dcols, tid);
         else
-            stage_tile_swz<MM_T, Cf::DT, Cf::SWM, MM_NT>(static_cast<float*>(dtile(slot, i)),
+            stage_tile_swz<MM_T, Cf::DT, Cf::SWM, NT>(static_cast<float*>(dtile(slot, i)),
                                                          reinterpret_cast<const float*>(g),
                                                          gstride, rows, dcols, vec, tid);
     }
@@ -307,11 +309,11 @@ struct MMStager {
             return;
         }
         if constexpr (Sm::WIDE)
-            stage_tile_b16<MM_T, N, N, MM_NT>(static_cast<uint16_t*>(ntile(slot, j)),
+            stage_tile_b16<MM_T, N, N, NT>(static_cast<uint16_t*>(ntile(slot, j)),
                                               reinterpret_cast<const uint16_t*>(g), gstride, rows,
                                               N, tid);
         else
-            stage_tile_swz<MM_T, N, 0, MM_NT>(static_cast<float*>(ntile(slot, j)),
+            stage_tile_swz<MM_T, N, 0, NT>(static_cast<float*>(ntile(slot, j)),
                                               reinterpret_cast<const float*>(g), gstride, rows,
                                               N, vec, tid);
     }
@@ -333,12 +335,12 @@ struct MMStager {
 #pragma unroll
             for (int i = 0; i < NDT; ++i)
                 if (dmask & (1u << i))
-                    widen_tile_swz<MM_T, Cf::DT, Cf::SWM, MM_NT>(smem + i * Cf::TR,
+                    widen_tile_swz<MM_T, Cf::DT, Cf::SWM, NT>(smem + i * Cf::TR,
                                                                  r + i * MM_T * Cf::DT, tid);
 #pragma unroll
             for (int j = 0; j < 2; ++j)
                 if (nmask & (1u << j))
-                    widen_tile_swz<MM_T, N, 0, MM_NT>(smem + NDT * Cf::TR + j * Cf::TN,
+                    widen_tile_swz<MM_T, N, 0, NT>(smem + NDT * Cf::TR + j * Cf::TN,
                                                       r + NDT * MM_T * Cf::DT + j * MM_T * N, tid);
             return smem;
         } else {
@@ -360,10 +362,10 @@ __device__ __forceinline__ void mm_pipe_init(uint64_t* bars, bool tma) {
 // ---------------------------------------------------------------------------
 // forward (SUMM: the segment summary instead -- no C, z, y or checkpoints)
 // ---------------------------------------------------------------------------
-template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, bool SUMM>
-__global__ void __launch_bounds__(MM_NT)
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, bool SUMM, int NT>
+__global__ void __launch_bounds__(NT)
     mmscan_fwd_kernel(const MMParams p, const __grid_constant__ MMTmaps tmaps) {
-    using Cf = MMCfg<N, NP>;
+    using Cf = MMCfg<N, NP, NT>;
     using ET = typename E::T;
     constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, IPL = Cf::IPL, LB = Cf::LB;
     constexpr int NP2 = Cf::NP2, NBLK = T / MM_CK;
@@ -371,7 +373,7 @@ __global__ void __launch_bounds__(MM_NT)
     extern __shared__ float4 smem4[];
     __shared__ uint64_t bars[MM_NS];
     // tiles: x | delta | z (T x DT), B | C (T x N)
-    MMStager<N, NP, 3, E> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0, p.vec, p.tma};
+    MMStager<N, NP, 3, E, NT> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0, p.vec, p.tma};
     mm_pipe_init(bars, p.tma);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -466,7 +468,7 @@ __global__ void __launch_bounds__(MM_NT)
             return;
         }
         st = stg.view(c % MM_NS, DMASK, NMASK);
-        if (MMSmem<N, NP, 3, E::BYTES>::WIDE) __syncthreads();
+        if (MMSmem<N, NP, 3, E::BYTES, NT>::WIDE) __syncthreads();
         const float* sx = st;
         const float* sdl = st + Cf::TR;
         const float* sz = st + 2 * Cf::TR;
@@ -621,8 +623,8 @@ __global__ void __launch_bounds__(MM_NT)
 
 // The backward sums dB | dC over the CTA's warps per chunk before the global
 // reductions (4x fewer atomics) when the chunk buffer fits: N <= 32.
-template <int N>
-__host__ __device__ constexpr bool mm_bwd_cbuf() { return N <= 32; }
+template <int N, int NT = MM_NT>
+__host__ __device__ constexpr bool mm_bwd_cbuf() { return N <= 32 && NT > 32; }
 
 // ---------------------------------------------------------------------------
 // backward
@@ -636,11 +638,11 @@ __host__ __device__ constexpr bool mm_bwd_cbuf() { return N <= 32; }
 // ---------------------------------------------------------------------------
 // (min 1 block per SM: without it ptxas caps the registers for 3 blocks per SM
 // and spills; the 254-register build measured 7-8 % faster)
-template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E>
-__global__ void __launch_bounds__(MM_NT, 1)
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, int NT>
+__global__ void __launch_bounds__(NT, 1)
     mmscan_bwd_kernel(const MMParams p, const __grid_constant__ MMTmaps tmaps) {
-    using Cf = MMCfg<N, NP>;
-    using Sm = MMSmem<N, NP, 4, E::BYTES>;
+    using Cf = MMCfg<N, NP, NT>;
+    using Sm = MMSmem<N, NP, 4, E::BYTES, NT>;
     using ET = typename E::T;
     constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, IPL = Cf::IPL, LB = Cf::LB;
     constexpr int NP2 = Cf::NP2, TR = Cf::TR, DPW = Cf::DPW;
@@ -649,12 +651,12 @@ __global__ void __launch_bounds__(MM_NT, 1)
     extern __shared__ float4 smem4[];
     __shared__ uint64_t bars[MM_NS];
     // tiles: x | delta | z | dout (T x DT), B | C (T x N); then the window buffer
-    MMStager<N, NP, 4, E> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0, p.vec, p.tma};
+    MMStager<N, NP, 4, E, NT> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0, p.vec, p.tma};
     mm_pipe_init(bars, p.tma);
     float* wbuf = stg.smem + Sm::FLOATS;
     // chunk buffer (N <= 32): each warp's d-sums of dB | dC for the 32 steps of
     // a chunk, [warp][step][2N]; summed over the CTA's warps once per chunk
-    constexpr bool CBUF = mm_bwd_cbuf<N>();
+    constexpr bool CBUF = mm_bwd_cbuf<N, NT>();
     float4* cbuf = reinterpret_cast<float4*>(wbuf + MM_CK * DT * 2 * N);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -940,11 +942,11 @@ __global__ void __launch_bounds__(MM_NT, 1)
             // to global memory per (step, 4 columns)
             constexpr int ITEMS = T * NQ;
 #pragma unroll
-            for (int i = tid; i < ITEMS; i += MM_NT) {
+            for (int i = tid; i < ITEMS; i += NT) {
                 const int s = i / NQ, q = i % NQ;
                 float2 a01 = f2(0.f), a23 = f2(0.f);
 #pragma unroll
-                for (int wi = 0; wi < MM_NT / 32; ++wi) {
+                for (int wi = 0; wi < NT / 32; ++wi) {
                     const float4 vv = cbuf[(wi * T + s) * NQ + q];
                     a01 = fadd2(a01, make_float2(vv.x, vv.y));
                     a23 = fadd2(a23, make_float2(vv.z, vv.w));
@@ -1131,9 +1133,9 @@ __global__ void __launch_bounds__(MM_NT)
 // Tensor maps of the activation and B/C tiles a launch stages; false (and the
 // kernel falls back to cp.async) when the rows are not 16-byte aligned or the
 // driver declines an encoding.
-template <int N, int NP, class E>
+template <int N, int NP, class E, int NT = MM_NT>
 bool mm_build_tmaps(const MMParams& p, MMTmaps& tm) {
-    using Cf = MMCfg<N, NP>;
+    using Cf = MMCfg<N, NP, NT>;
     if (!p.vec) return false;
     const int eb = E::BYTES;
     const int swz = eb == 4 ? Cf::SWB : 0;  // bf16 raw tiles land unswizzled
@@ -1157,42 +1159,55 @@ bool mm_build_tmaps(const MMParams& p, MMTmaps& tm) {
     return true;
 }
 
-template <int N, int NP, class E>
+template <int N, int NP, class E, int NT = MM_NT>
 MMParams mm_launch_params(const MMParams& p0, MMTmaps& tm) {
     MMParams p = p0;
-    p.tma = mm_build_tmaps<N, NP, E>(p, tm) ? 1 : 0;
+    p.tma = mm_build_tmaps<N, NP, E, NT>(p, tm) ? 1 : 0;
     p.err = mmb_device_error_flag();
     return p;
 }
 
+// CTA sizes of the forward and the backward: 128 threads (32 channels at
+// N = 16) or 32 threads (8 channels: four times the CTAs, so that the SMs'
+// shares of a small grid differ by at most one warp).
+#ifndef MMB_FWD_NT
+#define MMB_FWD_NT 128
+#endif
+#ifndef MMB_BWD_NT
+#define MMB_BWD_NT 32
+#endif
+
 template <int N, int NP, bool SP, bool Z, class E, bool SUMM>
 int launch_fwd_t(const MMParams& p0, cudaStream_t stream) {
-    using Cf = MMCfg<N, NP>;
-    const size_t smem = sizeof(float) * MMSmem<N, NP, 3, E::BYTES>::FLOATS + MM_SMEM_ALIGN;
+    constexpr int NT = (!SUMM && MMB_FWD_NT == 32 && 32 / (N / NP) >= 8) ? 32 : MM_NT;
+    using Cf = MMCfg<N, NP, NT>;
+    const size_t smem = sizeof(float) * MMSmem<N, NP, 3, E::BYTES, NT>::FLOATS + MM_SMEM_ALIGN;
     static int attr_done[MMB_MAX_DEVICES] = {};
-    const int st = mmb_smem_attr(mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM>, smem, attr_done);
+    const int st = mmb_smem_attr(mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM, NT>, smem, attr_done);
     if (st != MMB_OK) return st;
     MMTmaps tm;
-    const MMParams p = mm_launch_params<N, NP, E>(p0, tm);
+    const MMParams p = mm_launch_params<N, NP, E, NT>(p0, tm);
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
-    mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM><<<grid, MM_NT, smem, stream>>>(p, tm);
+    mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM, NT><<<grid, NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }
 
 template <int N, int NP, bool SP, bool Z, class E>
 int launch_bwd_t(const MMParams& p0, cudaStream_t stream) {
-    using Cf = MMCfg<N, NP>;
+    // 32 threads only where a CTA keeps at least 8 channels (32-byte tile rows)
+    constexpr int NT = (MMB_BWD_NT == 32 && 32 / (N / NP) >= 8) ? 32 : MM_NT;
+    using Cf = MMCfg<N, NP, NT>;
     const size_t smem =
-        sizeof(float) * (MMSmem<N, NP, 4, E::BYTES>::FLOATS + MM_CK * Cf::DT * 2 * N +
-                         (mm_bwd_cbuf<N>() ? (MM_NT / 32) * MM_T * 2 * N : 0)) +
+        sizeof(float) * (MMSmem<N, NP, 4, E::BYTES, NT>::FLOATS + MM_CK * Cf::DT * 2 * N +
+                         (mm_bwd_cbuf<N, NT>() ? (NT / 32) * MM_T * 2 * N : 0)) +
         MM_SMEM_ALIGN;
     static int attr_done[MMB_MAX_DEVICES] = {};
-    const int st = mmb_smem_attr(mmscan_bwd_kernel<N, NP, SP, Z, E>, smem, attr_done);
+    const int st = mmb_smem_attr(mmscan_bwd_kernel<N, NP, SP, Z, E, NT>, smem, attr_done);
     if (st != MMB_OK) return st;
     MMTmaps tm;
-    const MMParams p = mm_launch_params<N, NP, E>(p0, tm);
+    const MMParams p = mm_launch_params<N, NP, E, NT>(p0, tm);
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
-    mmscan_bwd_kernel<N, NP, SP, Z, E><<<grid, MM_NT, smem, stream>>>(p, tm);
+    mmscan_bwd_kernel<N, NP, SP, Z, E, NT><<<grid, NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }
 
