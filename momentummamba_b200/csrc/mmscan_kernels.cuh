@@ -1167,19 +1167,21 @@ MMParams mm_launch_params(const MMParams& p0, MMTmaps& tm) {
     return p;
 }
 
-// CTA sizes of the forward and the backward: 128 threads (32 channels at
-// N = 16) or 32 threads (8 channels: four times the CTAs, so that the SMs'
-// shares of a small grid differ by at most one warp).
-#ifndef MMB_FWD_NT
-#define MMB_FWD_NT 128
-#endif
+// CTA size of the backward: 32 threads (8 channels at N = 16, four times the
+// CTAs of 128-thread blocks, so that the SMs' shares of a small grid differ by
+// at most one warp; measured as fast or faster at larger batches too).
 #ifndef MMB_BWD_NT
 #define MMB_BWD_NT 32
 #endif
+// The forward picks its CTA size per call: 32 threads when 128-thread CTAs
+// would give the SMs fewer than MM_FWD_SMALL_CTAS_PER_SM each (the grid is too
+// small to balance), else 128 (more CTAs per SM for larger grids: 32-thread
+// CTAs measured 7-12 % slower at B=128-256, D=256).
+constexpr int MM_SMS = 148;
+constexpr int MM_FWD_SMALL_CTAS_PER_SM = 3;
 
-template <int N, int NP, bool SP, bool Z, class E, bool SUMM>
-int launch_fwd_t(const MMParams& p0, cudaStream_t stream) {
-    constexpr int NT = (!SUMM && MMB_FWD_NT == 32 && 32 / (N / NP) >= 8) ? 32 : MM_NT;
+template <int N, int NP, bool SP, bool Z, class E, bool SUMM, int NT>
+int launch_fwd_nt(const MMParams& p0, cudaStream_t stream) {
     using Cf = MMCfg<N, NP, NT>;
     const size_t smem = sizeof(float) * MMSmem<N, NP, 3, E::BYTES, NT>::FLOATS + MM_SMEM_ALIGN;
     static int attr_done[MMB_MAX_DEVICES] = {};
@@ -1190,6 +1192,18 @@ int launch_fwd_t(const MMParams& p0, cudaStream_t stream) {
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
     mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM, NT><<<grid, NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
+}
+
+template <int N, int NP, bool SP, bool Z, class E, bool SUMM>
+int launch_fwd_t(const MMParams& p0, cudaStream_t stream) {
+    // 32 threads only where a CTA keeps at least 8 channels (32-byte tile rows)
+    if constexpr (!SUMM && 32 / (N / NP) >= 8) {
+        constexpr int DT128 = MMCfg<N, NP, MM_NT>::DT;
+        const int64_t ctas = (p0.D + DT128 - 1) / DT128 * p0.Bsz;
+        if (ctas < (int64_t)MM_SMS * MM_FWD_SMALL_CTAS_PER_SM)
+            return launch_fwd_nt<N, NP, SP, Z, E, SUMM, 32>(p0, stream);
+    }
+    return launch_fwd_nt<N, NP, SP, Z, E, SUMM, MM_NT>(p0, stream);
 }
 
 template <int N, int NP, bool SP, bool Z, class E>
