@@ -158,31 +158,72 @@ __global__ void __launch_bounds__(LS_NT) ls_fwd_summary(const LSParams q) {
     rec[1] = make_float4(x1r, x1i, x2r, x2i);
 }
 
+// Chunk carries.  Across chunks the state follows x_{c+1} = K_c x_c + w_c, an
+// affine map per chunk (its transition product and its state from zero); a
+// warp takes 32 consecutive chunks of a chain and composes the maps with a
+// shuffle scan (Hillis-Steele) instead of one thread walking every chunk.
+struct LSAff {
+    LSMat m;
+    float x1r, x1i, x2r, x2i;
+};
+__device__ __forceinline__ LSAff ls_aff_shfl_up(const LSAff& v, int d) {
+    const unsigned F = 0xffffffffu;
+    return {{__shfl_up_sync(F, v.m.a, d), __shfl_up_sync(F, v.m.b, d),
+             __shfl_up_sync(F, v.m.c, d), __shfl_up_sync(F, v.m.d, d)},
+            __shfl_up_sync(F, v.x1r, d), __shfl_up_sync(F, v.x1i, d),
+            __shfl_up_sync(F, v.x2r, d), __shfl_up_sync(F, v.x2i, d)};
+}
+__device__ __forceinline__ LSAff ls_aff_shfl(const LSAff& v, int src) {
+    const unsigned F = 0xffffffffu;
+    return {{__shfl_sync(F, v.m.a, src), __shfl_sync(F, v.m.b, src),
+             __shfl_sync(F, v.m.c, src), __shfl_sync(F, v.m.d, src)},
+            __shfl_sync(F, v.x1r, src), __shfl_sync(F, v.x1i, src),
+            __shfl_sync(F, v.x2r, src), __shfl_sync(F, v.x2i, src)};
+}
+// the map `later` after the map `earlier`
+__device__ __forceinline__ LSAff ls_aff_then(const LSAff& later, const LSAff& earlier) {
+    const LSMat& m = later.m;
+    return {ls_mul(m, earlier.m),
+            m.a * earlier.x1r + m.b * earlier.x2r + later.x1r,
+            m.a * earlier.x1i + m.b * earlier.x2i + later.x1i,
+            m.c * earlier.x1r + m.d * earlier.x2r + later.x2r,
+            m.c * earlier.x1i + m.d * earlier.x2i + later.x2i};
+}
+// Exclusive scan over the warp's lanes of x_{l+1} = map_l(x_l) from x_0 = xin:
+// lane l gets x_l in `ex`; every lane gets x_32 back.
+__device__ __forceinline__ float4 ls_warp_carry(LSAff v, const float4& xin, int lane, float4& ex) {
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+        const LSAff o = ls_aff_shfl_up(v, 1 << k);
+        if (lane >= (1 << k)) v = ls_aff_then(v, o);
+    }
+    const LSAff prev = ls_aff_shfl_up(v, 1);  // maps of lanes 0 .. l-1
+    const LSAff x0 = {{0.f, 0.f, 0.f, 0.f}, xin.x, xin.y, xin.z, xin.w};
+    const LSAff e = lane ? ls_aff_then(prev, x0) : x0;
+    ex = make_float4(e.x1r, e.x1i, e.x2r, e.x2i);
+    const LSAff n = ls_aff_then(ls_aff_shfl(v, 31), x0);
+    return make_float4(n.x1r, n.x1i, n.x2r, n.x2i);
+}
+
 // per (b, p): the state entering each chunk; overwrites the record's x with it
 __global__ void __launch_bounds__(LS_NT) ls_fwd_carry(const LSParams q) {
-    const int64_t idx = (int64_t)blockIdx.x * LS_NT + threadIdx.x;
-    if (idx >= q.Bsz * q.PP) return;
-    const int64_t p = idx % q.PP, b = idx / q.PP;
+    const int64_t chain = (int64_t)blockIdx.x * (LS_NT / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (chain >= q.Bsz * q.PP) return;  // whole warps
+    const int64_t p = chain % q.PP, b = chain / q.PP;
     float4* tab = reinterpret_cast<float4*>(ls_tab(q));
-    float x1r = 0.f, x1i = 0.f, x2r = 0.f, x2i = 0.f;
-    for (int64_t c0 = 0; c0 < q.C; c0 += 4) {
-        float4 mm[4], xs[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {  // records past the end: the last one again (unused)
-            const int64_t r = (b * q.C + (c0 + i < q.C ? c0 + i : q.C - 1)) * q.PP + p;
-            mm[i] = tab[r * 2];
-            xs[i] = tab[r * 2 + 1];
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t c0 = 0; c0 < q.C; c0 += 32) {
+        const int64_t c = c0 + lane;
+        LSAff v = {{1.f, 0.f, 0.f, 1.f}, 0.f, 0.f, 0.f, 0.f};
+        const int64_t r = (b * q.C + c) * q.PP + p;
+        if (c < q.C) {
+            const float4 mm = tab[r * 2], xs = tab[r * 2 + 1];
+            v = {{mm.x, mm.y, mm.z, mm.w}, xs.x, xs.y, xs.z, xs.w};
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            if (c0 + i >= q.C) break;
-            tab[((b * q.C + c0 + i) * q.PP + p) * 2 + 1] = make_float4(x1r, x1i, x2r, x2i);
-            const float n1r = mm[i].x * x1r + mm[i].y * x2r + xs[i].x;
-            const float n1i = mm[i].x * x1i + mm[i].y * x2i + xs[i].y;
-            const float n2r = mm[i].z * x1r + mm[i].w * x2r + xs[i].z;
-            const float n2i = mm[i].z * x1i + mm[i].w * x2i + xs[i].w;
-            x1r = n1r; x1i = n1i; x2r = n2r; x2i = n2i;
-        }
+        float4 ex;
+        x = ls_warp_carry(v, x, lane, ex);
+        if (c < q.C) tab[r * 2 + 1] = ex;
     }
 }
 
@@ -277,36 +318,32 @@ __global__ void __launch_bounds__(LS_NT) ls_bwd_summary(const LSParams q) {
 }
 
 // per (b, p), chunks in reverse: mu_c = M_{t0(c+1)}^T lam_{t0(c+1)} entering chunk c
-// from the right; written to the record's last float4.
+// from the right; written to the record's last float4.  With lam_{t0} = lam_loc
+// + Q mu, mu_{c-1} = M_{t0}^T Q mu_c + M_{t0}^T lam_loc: an affine map per chunk,
+// scanned by one warp per chain over 32 chunks at a time from the last.
 __global__ void __launch_bounds__(LS_NT) ls_bwd_carry(const LSParams q) {
-    const int64_t idx = (int64_t)blockIdx.x * LS_NT + threadIdx.x;
-    if (idx >= q.Bsz * q.PP) return;
-    const int64_t p = idx % q.PP, b = idx / q.PP;
+    const int64_t chain = (int64_t)blockIdx.x * (LS_NT / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (chain >= q.Bsz * q.PP) return;  // whole warps
+    const int64_t p = chain % q.PP, b = chain / q.PP;
     float4* tab = reinterpret_cast<float4*>(ls_tab(q));
-    float m1r = 0.f, m1i = 0.f, m2r = 0.f, m2i = 0.f;
-    for (int64_t c0 = q.C - 1; c0 >= 0; c0 -= 4) {
-        float4 lam[4], Qv[4], m0[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {  // records before the start: chunk 0 again (unused)
-            const int64_t r = (b * q.C + (c0 - i >= 0 ? c0 - i : 0)) * q.PP + p;
-            lam[i] = tab[r * 4];
-            Qv[i] = tab[r * 4 + 1];
-            m0[i] = tab[r * 4 + 2];
+    float4 mu = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int64_t r0 = 0; r0 < q.C; r0 += 32) {
+        const int64_t c = q.C - 1 - (r0 + lane);  // lanes take chunks from the last
+        LSAff v = {{1.f, 0.f, 0.f, 1.f}, 0.f, 0.f, 0.f, 0.f};
+        const int64_t r = (b * q.C + c) * q.PP + p;
+        if (c >= 0) {
+            const float4 lam = tab[r * 4], Q = tab[r * 4 + 1], M = tab[r * 4 + 2];
+            const LSMat mt = {M.x, M.z, M.y, M.w};  // M_{t0}^T
+            v.m = ls_mul(mt, LSMat{Q.x, Q.y, Q.z, Q.w});
+            v.x1r = mt.a * lam.x + mt.b * lam.z;
+            v.x1i = mt.a * lam.y + mt.b * lam.w;
+            v.x2r = mt.c * lam.x + mt.d * lam.z;
+            v.x2i = mt.c * lam.y + mt.d * lam.w;
         }
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            if (c0 - i < 0) break;
-            tab[((b * q.C + c0 - i) * q.PP + p) * 4 + 3] = make_float4(m1r, m1i, m2r, m2i);
-            // lam_{t0} = lam_loc + Q mu ; mu for the previous chunk = M_{t0}^T lam_{t0}
-            const float4 Q = Qv[i];
-            const float a1r = Q.x * m1r + Q.y * m2r + lam[i].x;
-            const float a1i = Q.x * m1i + Q.y * m2i + lam[i].y;
-            const float a2r = Q.z * m1r + Q.w * m2r + lam[i].z;
-            const float a2i = Q.z * m1i + Q.w * m2i + lam[i].w;
-            const float4 M = m0[i];  // M_{t0} = [[x, y], [z, w]]; apply its transpose
-            m1r = M.x * a1r + M.z * a2r; m1i = M.x * a1i + M.z * a2i;
-            m2r = M.y * a1r + M.w * a2r; m2i = M.y * a1i + M.w * a2i;
-        }
+        float4 ex;
+        mu = ls_warp_carry(v, mu, lane, ex);
+        if (c >= 0) tab[r * 4 + 3] = ex;
     }
 }
 
@@ -459,7 +496,7 @@ extern "C" int mmb_linoss_sel_fwd(int32_t disc, int64_t batch, int64_t L, int64_
         return MMB_ERR_LAUNCH;
     }
     ls_fwd_summary<<<ls_blocks(q.Bsz * q.C * q.PP), LS_NT, 0, cs>>>(q);
-    ls_fwd_carry<<<ls_blocks(q.Bsz * q.PP), LS_NT, 0, cs>>>(q);
+    ls_fwd_carry<<<ls_blocks(q.Bsz * q.PP * 32), LS_NT, 0, cs>>>(q);
     ls_fwd_final<<<ls_blocks(q.Bsz * q.C * q.PP), LS_NT, 0, cs>>>(q);
     return mmb_launch_status();
 }
@@ -486,7 +523,7 @@ extern "C" int mmb_linoss_sel_bwd(int32_t disc, int64_t batch, int64_t L, int64_
         return MMB_ERR_LAUNCH;
     }
     ls_bwd_summary<<<ls_blocks(q.Bsz * q.C * q.PP), LS_NT, 0, cs>>>(q);
-    ls_bwd_carry<<<ls_blocks(q.Bsz * q.PP), LS_NT, 0, cs>>>(q);
+    ls_bwd_carry<<<ls_blocks(q.Bsz * q.PP * 32), LS_NT, 0, cs>>>(q);
     ls_bwd_final<<<ls_blocks(q.Bsz * q.C * q.PP), LS_NT, 0, cs>>>(q);
     return mmb_launch_status();
 }
