@@ -812,6 +812,139 @@ def run_linoss(args):
     }
 
 
+# ---------------------------------------------------------------------------
+# row-form and PScan-layout scans (the reference's materialised-tensor paths)
+# ---------------------------------------------------------------------------
+def run_rows(args):
+    """The momentum row scan (momentum_scan_cuda.py:204-253: R = B*D*N rows of L
+    steps) and the diagonal scan in the PScan layout (pscan.py:43-234: (B, L,
+    D*N)) forward + backward at the stack's size (B=32, L=1024, D=256, N=16:
+    134,217,728 elements each).  One step = rows fwd + bwd, then pscan fwd + bwd;
+    elements = the rows scan's (the line's value), per-kernel GB/s for both.
+    Batch-sharded replicas over ranks (weak)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from momentummamba_b200 import _lib
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    lib = _lib.load()
+    R, L, M = BSZ * DIM * DST, SEQ, DIM * DST
+    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    a = torch.exp(-torch.rand(R, L, device=dev, generator=g) * 0.2)     # decay factors in (0.82, 1]
+    u = torch.randn(R, L, device=dev, generator=g)
+    gr = torch.randn(R, L, device=dev, generator=g)
+    h, da, du = torch.empty_like(a), torch.empty_like(a), torch.empty_like(a)
+    A3, X3, G3 = a.view(BSZ, L, M), u.view(BSZ, L, M), gr.view(BSZ, L, M)  # same bytes, PScan layout
+    H3, dA3, dX3 = torch.empty_like(A3), torch.empty_like(A3), torch.empty_like(A3)
+    Pp = _lib.ptr
+
+    def rows_fwd():
+        _lib.check(lib.mmb_rows_fwd(R, L, Pp(a), BETA, Pp(u), Pp(h), None, _lib.stream_of(a)),
+                   "rows fwd")
+
+    def rows_bwd():
+        _lib.check(lib.mmb_rows_bwd(R, L, Pp(gr), Pp(a), BETA, Pp(h), Pp(da), Pp(du),
+                                    _lib.stream_of(a)), "rows bwd")
+
+    def ps_fwd():
+        _lib.check(lib.mmb_pscan_fwd(BSZ, L, M, Pp(A3), Pp(X3), Pp(H3), _lib.stream_of(a)),
+                   "pscan fwd")
+
+    def ps_bwd():
+        _lib.check(lib.mmb_pscan_bwd(BSZ, L, M, Pp(A3), Pp(H3), Pp(G3), Pp(dA3), Pp(dX3),
+                                     _lib.stream_of(a)), "pscan bwd")
+
+    def stepfn():
+        rows_fwd()
+        rows_bwd()
+        ps_fwd()
+        ps_bwd()
+
+    for _ in range(max(3, args.warmup)):
+        stepfn()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cs = torch.cuda.Stream(device=dev)
+    cs.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cs):
+        with torch.cuda.graph(graph, stream=cs):
+            stepfn()
+    torch.cuda.current_stream().wait_stream(cs)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.5)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    reps = 10
+    t = {}
+    cur = torch.cuda.current_stream()
+    for name, fn in (("rows_fwd", rows_fwd), ("rows_bwd", rows_bwd), ("pscan_fwd", ps_fwd),
+                     ("pscan_bwd", ps_bwd)):
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for e_a, e_b in evs:
+            e_a.record(cur)
+            fn()
+            e_b.record(cur)
+        torch.cuda.synchronize()
+        t[name] = statistics.mean(x.elapsed_time(y) for x, y in evs)
+    del graph
+    if world > 1:
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
+    elems = R * L
+    nbytes = {"rows_fwd": 12 * elems, "rows_bwd": 20 * elems,   # a, u -> h; g, a, h -> da, du
+              "pscan_fwd": 12 * elems, "pscan_bwd": 20 * elems}  # A, X -> H; A, H, G -> dA, dX
+    peak, peak_kind = load_peaks()
+    kern = {k: {"ms": v, "algorithmic_bytes": nbytes[k], "GB/s": nbytes[k] / (v / 1e3) / 1e9,
+                "frac": nbytes[k] / (v / 1e3) / 1e9 / peak} for k, v in t.items()}
+    return {
+        "metric": METRIC, "value": job_rate(elems * args.steps, world, ms), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "materialised-tensor scans at the stack's size: momentum row scan "
+                               "(R=131072 rows x L=1024, beta 0.6) and PScan-layout diagonal scan "
+                               "(B=32 L=1024 M=4096), fwd+bwd each; value = row-scan elements/s "
+                               "over the whole step",
+                   "parallelism": f"batch-sharded x{world}", "launch": "cuda graph",
+                   "l2": "inputs larger than L2 (537 MB per tensor)"},
+        "roofline": {"kernel": "rows_bwd", "bound": "hbm", "achieved": kern["rows_bwd"]["GB/s"],
+                     "peak": peak, "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s",
+                     "frac": kern["rows_bwd"]["frac"], "algorithmic_bytes": nbytes["rows_bwd"],
+                     "ms_per_launch": t["rows_bwd"], "traffic": None},
+        "kernels": kern,
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks,
+    }
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -826,10 +959,11 @@ def main():
                     help="run warm-up and steps eagerly and exit (for profiler captures)")
     ap.add_argument("--batch", type=int, default=BSZ,
                     help="sequences per layer (profiling only; the benchmark line uses 32)")
-    ap.add_argument("--workload", choices=["stack", "long", "linoss"], default="stack",
+    ap.add_argument("--workload", choices=["stack", "long", "linoss", "rows"], default="stack",
                     help="stack: the 4-layer MambaMomentum scan (batch-sharded, the benchmark "
                          "line); long: B=8 L=65536 D=2048 bf16, sequence-sharded; linoss: the "
-                         "LinOSS layer scan, IM and IMEX, B=16 L=4096 P=256")
+                         "LinOSS layer scan, IM and IMEX, B=16 L=4096 P=256; rows: the "
+                         "row-form and PScan-layout scans at the stack's size")
     ap.add_argument("--phases", action="store_true",
                     help="long workload: also time each phase (adds events to the step)")
     args = ap.parse_args()
@@ -840,6 +974,8 @@ def main():
         line = run_long(args)
     elif args.workload == "linoss":
         line = run_linoss(args)
+    elif args.workload == "rows":
+        line = run_rows(args)
     else:
         line = run_b200(args)
     if line is not None:
