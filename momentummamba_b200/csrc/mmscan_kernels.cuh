@@ -802,7 +802,8 @@ __global__ void __launch_bounds__(NT, 1)
                     aa[s][j] = make_float2(ex2(e.x), ex2(e.y));
                 }
             }
-            // forward replay of the window
+            // forward replay of the window (states only: the gate's y = C h is
+            // formed in the adjoint sweep, from the C it loads anyway)
             float2 hh[MM_CK + 1][NP2];
             float yv[MM_CK];
 #pragma unroll
@@ -810,18 +811,15 @@ __global__ void __launch_bounds__(NT, 1)
 #pragma unroll
             for (int s = 0; s < MM_CK; ++s) {
                 const int tt = w0 + s;
-                float2 bq[NP2], cq[NP2];
+                float2 bq[NP2];
                 ld_pairs<NP>(sB + tt * N + ng * NP, bq);
-                ld_pairs<NP>(sC + tt * N + ng * NP, cq);
 #pragma unroll
                 for (int j = 0; j < NP2; ++j) {
                     v[j] = ffma2(beta2, v[j], fmul2(f2(dtxs[s]), bq[j]));
                     h[j] = ffma2(aa[s][j], h[j], v[j]);
                     hh[s + 1][j] = h[j];
                 }
-                yv[s] = dot_pairs(cq, h);
             }
-            reduce_scatter<MM_CK, 0, Cf::LOG2G>(yv, lane);
             float dys[MM_CK];
 #pragma unroll
             for (int s = 0; s < MM_CK; ++s) {
@@ -837,6 +835,7 @@ __global__ void __launch_bounds__(NT, 1)
                 float2 bq[NP2], cq[NP2];
                 ld_pairs<NP>(sB + tt * N + ng * NP, bq);
                 ld_pairs<NP>(sC + tt * N + ng * NP, cq);
+                if (HAS_Z) yv[s] = dot_pairs(cq, hh[s + 1]);
                 const float2 dy2 = f2(dys[s]);
                 float2 sb = f2(0.f), sa = f2(0.f), pb[NP2], pc[NP2];
 #pragma unroll
@@ -866,6 +865,7 @@ __global__ void __launch_bounds__(NT, 1)
                 }
             }
             // n-sums back to the owning lanes: sab[2i], sab[2i + 1] = (SA, SB) of item i
+            if (HAS_Z) reduce_scatter<MM_CK, 0, Cf::LOG2G>(yv, lane);
             reduce_scatter<2 * MM_CK, 0, Cf::LOG2G>(sab, lane);
             if (G == 16) sab[1] = __shfl_xor_sync(FULL, sab[0], 8);
 #pragma unroll
