@@ -770,8 +770,9 @@ __global__ void __launch_bounds__(NT, 1)
                 v[j] = nck_v[j];
             }
             if (t0 + w0 > 0) ck_next();
-            // this lane's items: dt, alpha*dt*x, dy = dout*silu(z)
-            float xi[IPL], ri[IPL], dti[IPL], dtxi[IPL], dyi[IPL];
+            // this lane's items: dt, alpha*dt*x, dy = dout*silu(z), and the gate's
+            // dz / (y + D x) = dout * sigmoid(z) * (1 + z (1 - sigmoid(z)))
+            float xi[IPL], ri[IPL], dti[IPL], dtxi[IPL], dyi[IPL], gzi[IPL];
 #pragma unroll
             for (int i = 0; i < IPL; ++i) {
                 const int row = Cf::dix(w0 + ibase + i, dl);
@@ -780,9 +781,12 @@ __global__ void __launch_bounds__(NT, 1)
                 dti[i] = SOFTPLUS ? softplus_f(ri[i]) : ri[i];
                 dtxi[i] = alpha * dti[i] * xi[i];
                 float dy = sdo[row];
+                gzi[i] = 0.f;
                 if (HAS_Z) {
                     const float zv = sz[row];
-                    dy *= zv * sigmoid_f(zv);
+                    const float sg = sigmoid_f(zv);
+                    gzi[i] = dy * sg * (1.f + zv * (1.f - sg));
+                    dy *= zv * sg;
                 }
                 dyi[i] = dy;
             }
@@ -878,10 +882,7 @@ __global__ void __launch_bounds__(NT, 1)
                 const float SB = sab[2 * i + 1];
                 const float xv = xi[i];
                 if (HAS_Z) {
-                    const float zv = sz[Cf::dix(tt, dl)];
-                    const float sg = sigmoid_f(zv);
-                    const float yfull = fmaf(Dv, xv, yv[i]);
-                    const float gz = sdo[Cf::dix(tt, dl)] * yfull * sg * (1.f + zv * (1.f - sg));
+                    const float gz = gzi[i] * fmaf(Dv, xv, yv[i]);
                     if (ok && gdz) E::store(gdz, gi, gz);
                 }
                 float gdt = fmaf(alpha * xv, SB, SA);
