@@ -234,6 +234,12 @@ __device__ __forceinline__ float softplus_grad(float r) {
     return r >= 0.f ? inv : w * inv;
 }
 
+// the same from w = e^{-|r|} as softplus_w returned it
+__device__ __forceinline__ float softplus_grad_w(float r, float w) {
+    const float inv = rcp_approx(1.f + w);
+    return r >= 0.f ? inv : w * inv;
+}
+
 __device__ __forceinline__ float sigmoid_f(float r) {
     return rcp_approx(1.f + ex2(-r * MMB_LOG2E));
 }

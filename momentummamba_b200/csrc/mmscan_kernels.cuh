@@ -772,13 +772,14 @@ __global__ void __launch_bounds__(NT, 1)
             if (t0 + w0 > 0) ck_next();
             // this lane's items: dt, alpha*dt*x, dy = dout*silu(z), and the gate's
             // dz / (y + D x) = dout * sigmoid(z) * (1 + z (1 - sigmoid(z)))
-            float xi[IPL], ri[IPL], dti[IPL], dtxi[IPL], dyi[IPL], gzi[IPL];
+            float xi[IPL], ri[IPL], wi[IPL], dti[IPL], dtxi[IPL], dyi[IPL], gzi[IPL];
 #pragma unroll
             for (int i = 0; i < IPL; ++i) {
                 const int row = Cf::dix(w0 + ibase + i, dl);
                 xi[i] = sx[row];
                 ri[i] = sdl[row] + bias_d;
-                dti[i] = SOFTPLUS ? softplus_f(ri[i]) : ri[i];
+                wi[i] = 0.f;  // e^{-|r|}, kept for the softplus derivative
+                dti[i] = SOFTPLUS ? softplus_w(ri[i], wi[i]) : ri[i];
                 dtxi[i] = alpha * dti[i] * xi[i];
                 float dy = sdo[row];
                 gzi[i] = 0.f;
@@ -886,7 +887,7 @@ __global__ void __launch_bounds__(NT, 1)
                     if (ok && gdz) E::store(gdz, gi, gz);
                 }
                 float gdt = fmaf(alpha * xv, SB, SA);
-                if (SOFTPLUS) gdt *= softplus_grad(ri[i]);
+                if (SOFTPLUS) gdt *= softplus_grad_w(ri[i], wi[i]);
                 if (ok) {
                     E::store(gdx, gi, fmaf(dyi[i], Dv, alpha * dti[i] * SB));
                     E::store(gddl, gi, gdt);
