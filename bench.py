@@ -808,6 +808,9 @@ def run_linoss(args):
         "kernels": {k: {"ms": v, "algorithmic_bytes": fwd_b if k.startswith("fwd") else bwd_b,
                         "GB/s": (fwd_b if k.startswith("fwd") else bwd_b) / (v / 1e3) / 1e9}
                     for k, v in t.items()},
+        # per discretisation: forward summary, carry, final; backward summary, carry,
+        # final, parameter chain rule
+        "gpu_launches": 14 * args.steps,
         "clocks": clocks,
     }
 
