@@ -162,46 +162,15 @@ __global__ void __launch_bounds__(LS_NT) ls_fwd_summary(const LSParams q) {
 // affine map per chunk (its transition product and its state from zero); a
 // warp takes 32 consecutive chunks of a chain and composes the maps with a
 // shuffle scan (Hillis-Steele) instead of one thread walking every chunk.
-struct LSAff {
-    LSMat m;
-    float x1r, x1i, x2r, x2i;
-};
-__device__ __forceinline__ LSAff ls_aff_shfl_up(const LSAff& v, int d) {
-    const unsigned F = 0xffffffffu;
-    return {{__shfl_up_sync(F, v.m.a, d), __shfl_up_sync(F, v.m.b, d),
-             __shfl_up_sync(F, v.m.c, d), __shfl_up_sync(F, v.m.d, d)},
-            __shfl_up_sync(F, v.x1r, d), __shfl_up_sync(F, v.x1i, d),
-            __shfl_up_sync(F, v.x2r, d), __shfl_up_sync(F, v.x2i, d)};
-}
-__device__ __forceinline__ LSAff ls_aff_shfl(const LSAff& v, int src) {
-    const unsigned F = 0xffffffffu;
-    return {{__shfl_sync(F, v.m.a, src), __shfl_sync(F, v.m.b, src),
-             __shfl_sync(F, v.m.c, src), __shfl_sync(F, v.m.d, src)},
-            __shfl_sync(F, v.x1r, src), __shfl_sync(F, v.x1i, src),
-            __shfl_sync(F, v.x2r, src), __shfl_sync(F, v.x2i, src)};
-}
-// the map `later` after the map `earlier`
-__device__ __forceinline__ LSAff ls_aff_then(const LSAff& later, const LSAff& earlier) {
-    const LSMat& m = later.m;
-    return {ls_mul(m, earlier.m),
-            m.a * earlier.x1r + m.b * earlier.x2r + later.x1r,
-            m.a * earlier.x1i + m.b * earlier.x2i + later.x1i,
-            m.c * earlier.x1r + m.d * earlier.x2r + later.x2r,
-            m.c * earlier.x1i + m.d * earlier.x2i + later.x2i};
-}
+using LSAff = Aff2<LSMat>;
 // Exclusive scan over the warp's lanes of x_{l+1} = map_l(x_l) from x_0 = xin:
 // lane l gets x_l in `ex`; every lane gets x_32 back.
-__device__ __forceinline__ float4 ls_warp_carry(LSAff v, const float4& xin, int lane, float4& ex) {
-#pragma unroll
-    for (int k = 0; k < 5; ++k) {
-        const LSAff o = ls_aff_shfl_up(v, 1 << k);
-        if (lane >= (1 << k)) v = ls_aff_then(v, o);
-    }
-    const LSAff prev = ls_aff_shfl_up(v, 1);  // maps of lanes 0 .. l-1
+__device__ __forceinline__ float4 ls_warp_carry(const LSAff& v, const float4& xin, int lane,
+                                                float4& ex) {
     const LSAff x0 = {{0.f, 0.f, 0.f, 0.f}, xin.x, xin.y, xin.z, xin.w};
-    const LSAff e = lane ? ls_aff_then(prev, x0) : x0;
+    LSAff e;
+    const LSAff n = warp_aff2_exscan(v, x0, lane, e);
     ex = make_float4(e.x1r, e.x1i, e.x2r, e.x2i);
-    const LSAff n = ls_aff_then(ls_aff_shfl(v, 31), x0);
     return make_float4(n.x1r, n.x1i, n.x2r, n.x2i);
 }
 

@@ -331,6 +331,63 @@ __device__ __forceinline__ int rs_index(int bits, int i) {
     return base + i;
 }
 
+// ---------------------------------------------------------------------------
+// Affine maps x -> M x + w on complex 2-vectors (x1, x2), M a real 2x2 matrix
+// type with members a, b, c, d ([[a, b], [c, d]]), and their composition
+// across a warp's lanes: the chunk carries of the 2x2 scans, one chunk per lane.
+// ---------------------------------------------------------------------------
+template <class Mt>
+struct Aff2 {
+    Mt m;
+    float x1r, x1i, x2r, x2i;
+};
+template <class Mt>
+__device__ __forceinline__ Mt mat2_mul(const Mt& x, const Mt& y) {
+    return {x.a * y.a + x.b * y.c, x.a * y.b + x.b * y.d, x.c * y.a + x.d * y.c,
+            x.c * y.b + x.d * y.d};
+}
+// the map `later` after the map `earlier`
+template <class Mt>
+__device__ __forceinline__ Aff2<Mt> aff2_then(const Aff2<Mt>& later, const Aff2<Mt>& earlier) {
+    const Mt& m = later.m;
+    return {mat2_mul(m, earlier.m),
+            m.a * earlier.x1r + m.b * earlier.x2r + later.x1r,
+            m.a * earlier.x1i + m.b * earlier.x2i + later.x1i,
+            m.c * earlier.x1r + m.d * earlier.x2r + later.x2r,
+            m.c * earlier.x1i + m.d * earlier.x2i + later.x2i};
+}
+template <class Mt>
+__device__ __forceinline__ Aff2<Mt> aff2_shfl_up(const Aff2<Mt>& v, int d) {
+    const unsigned F = 0xffffffffu;
+    return {{__shfl_up_sync(F, v.m.a, d), __shfl_up_sync(F, v.m.b, d),
+             __shfl_up_sync(F, v.m.c, d), __shfl_up_sync(F, v.m.d, d)},
+            __shfl_up_sync(F, v.x1r, d), __shfl_up_sync(F, v.x1i, d),
+            __shfl_up_sync(F, v.x2r, d), __shfl_up_sync(F, v.x2i, d)};
+}
+template <class Mt>
+__device__ __forceinline__ Aff2<Mt> aff2_shfl(const Aff2<Mt>& v, int src) {
+    const unsigned F = 0xffffffffu;
+    return {{__shfl_sync(F, v.m.a, src), __shfl_sync(F, v.m.b, src),
+             __shfl_sync(F, v.m.c, src), __shfl_sync(F, v.m.d, src)},
+            __shfl_sync(F, v.x1r, src), __shfl_sync(F, v.x1i, src),
+            __shfl_sync(F, v.x2r, src), __shfl_sync(F, v.x2i, src)};
+}
+// Exclusive scan of the lanes' maps applied after `in` (a map: the product of
+// the earlier chunks' matrices and the state they leave): lane l receives
+// map_{l-1} o ... o map_0 o in; every lane gets map_31 o ... o map_0 o in back.
+template <class Mt>
+__device__ __forceinline__ Aff2<Mt> warp_aff2_exscan(Aff2<Mt> v, const Aff2<Mt>& in, int lane,
+                                                     Aff2<Mt>& ex) {
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {  // Hillis-Steele: v <- maps of lanes (l - 2^(k+1), l]
+        const Aff2<Mt> o = aff2_shfl_up(v, 1 << k);
+        if (lane >= (1 << k)) v = aff2_then(v, o);
+    }
+    const Aff2<Mt> prev = aff2_shfl_up(v, 1);  // maps of lanes 0 .. l-1
+    ex = lane ? aff2_then(prev, in) : in;
+    return aff2_then(aff2_shfl(v, 31), in);
+}
+
 // Vector reduction-add of 4 consecutive floats in global memory (sm_90+).
 __device__ __forceinline__ void red_add_v4(float* gaddr, float a, float b, float c, float d) {
     asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};\n" ::"l"(gaddr), "f"(a), "f"(b),

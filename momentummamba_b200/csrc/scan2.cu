@@ -128,41 +128,34 @@ __global__ void __launch_bounds__(S2_NT) s2_fwd_summary(const S2Params p) {
     }
 }
 
+// Per (b, p) chain: the state entering each chunk and (MSCAN) the product of
+// the earlier chunks' matrices.  Chunk c's map is x -> Mprod_c x + x_loc_c; a
+// warp composes 32 consecutive chunks' maps with a shuffle scan.
 template <int NC, bool MSCAN>
 __global__ void __launch_bounds__(S2_NT) s2_fwd_carry(const S2Params p) {
-    const int64_t idx = (int64_t)blockIdx.x * S2_NT + threadIdx.x;
-    if (idx >= p.Bsz * p.P) return;
-    const int64_t j = idx % p.P, b = idx / p.P;
-    float x1[NC], x2[NC];
-#pragma unroll
-    for (int k = 0; k < NC; ++k) x1[k] = x2[k] = 0.f;
-    Mat2 pre = mident();
+    const int64_t chain = (int64_t)blockIdx.x * (S2_NT / 32) + threadIdx.x / 32;
+    const int lane = threadIdx.x & 31;
+    if (chain >= p.Bsz * p.P) return;  // whole warps
+    const int64_t j = chain % p.P, b = chain / p.P;
     const float* __restrict__ summ = p.work;
     float* __restrict__ carry = p.work + p.Bsz * p.C * p.P * S2_REC;
-    for (int64_t c0 = 0; c0 < p.C; c0 += S2_W) {
-        float4 sm[S2_W], sx[S2_W];  // the records: [Mprod | x_loc]
-#pragma unroll
-        for (int i = 0; i < S2_W; ++i) {  // records past the end: the last one again (unused)
-            const int64_t ci = c0 + i < p.C ? c0 + i : p.C - 1;
-            const float4* r = reinterpret_cast<const float4*>(summ + ((b * p.C + ci) * p.P + j) * S2_REC);
-            sm[i] = r[0];
-            sx[i] = r[1];
+    Aff2<Mat2> in = {mident(), 0.f, 0.f, 0.f, 0.f};
+    for (int64_t c0 = 0; c0 < p.C; c0 += 32) {
+        const int64_t c = c0 + lane;
+        Aff2<Mat2> v = {mident(), 0.f, 0.f, 0.f, 0.f};
+        const int64_t rec = ((b * p.C + c) * p.P + j) * S2_REC;
+        if (c < p.C) {  // record: [Mprod | x1, x2 (real) | x1, x2 (imaginary)]
+            const float4 sm = reinterpret_cast<const float4*>(summ + rec)[0];
+            const float4 sx = reinterpret_cast<const float4*>(summ + rec)[1];
+            v = {{sm.x, sm.y, sm.z, sm.w}, sx.x, NC > 1 ? sx.z : 0.f, sx.y, NC > 1 ? sx.w : 0.f};
         }
-#pragma unroll
-        for (int i = 0; i < S2_W; ++i) {
-            if (c0 + i >= p.C) break;
-            float4* out = reinterpret_cast<float4*>(carry + ((b * p.C + c0 + i) * p.P + j) * S2_REC);
-            out[0] = make_float4(pre.a, pre.b, pre.c, pre.d);
-            out[1] = make_float4(x1[0], x2[0], NC > 1 ? x1[NC - 1] : 0.f, NC > 1 ? x2[NC - 1] : 0.f);
-            const Mat2 mc = {sm[i].x, sm[i].y, sm[i].z, sm[i].w};
-            const float sl[4] = {sx[i].x, sx[i].y, sx[i].z, sx[i].w};
-#pragma unroll
-            for (int k = 0; k < NC; ++k) {
-                mvec(mc, x1[k], x2[k]);
-                x1[k] += sl[2 * k];
-                x2[k] += sl[2 * k + 1];
-            }
-            if (MSCAN) pre = mmul(mc, pre);
+        Aff2<Mat2> ex;
+        in = warp_aff2_exscan(v, in, lane, ex);
+        if (c < p.C) {
+            float4* out = reinterpret_cast<float4*>(carry + rec);
+            out[0] = MSCAN ? make_float4(ex.m.a, ex.m.b, ex.m.c, ex.m.d)
+                           : make_float4(1.f, 0.f, 0.f, 1.f);
+            out[1] = make_float4(ex.x1r, ex.x2r, NC > 1 ? ex.x1i : 0.f, NC > 1 ? ex.x2i : 0.f);
         }
     }
 }
@@ -818,7 +811,7 @@ static unsigned s2_blocks(int64_t n) { return (unsigned)((n + S2_NT - 1) / S2_NT
 template <int NC, bool MS>
 static int s2_fwd_launch(const S2Params& p, cudaStream_t st) {
     s2_fwd_summary<NC, MS><<<s2_blocks(p.Bsz * p.C * p.P), S2_NT, 0, st>>>(p);
-    s2_fwd_carry<NC, MS><<<s2_blocks(p.Bsz * p.P), S2_NT, 0, st>>>(p);
+    s2_fwd_carry<NC, MS><<<s2_blocks(p.Bsz * p.P * 32), S2_NT, 0, st>>>(p);
     s2_fwd_final<NC, MS><<<s2_blocks(p.Bsz * p.C * p.P), S2_NT, 0, st>>>(p);
     return mmb_launch_status();
 }
