@@ -1,22 +1,33 @@
 #!/usr/bin/env python
 """Benchmark of the momentum selective scan hot path on B200.
 
-Workload (one "step"): the scan of a 4-layer MambaMomentum stack, forward and
-backward -- per layer B=32 sequences, L=1024, D=256 channels (d_model 128 x
-expand 2), N=16 states, with the block's softplus(delta + bias) and SiLU(z) gate
-fused into the kernels.  Metric: scan elements (B*L*D*N) per second, fwd+bwd,
-summed over all GPUs.  Multi-GPU runs are batch-sharded (weak scaling): every
-rank scans its own 32 sequences per layer; the data path has no collective.
+Default line (one "step"): the scan of the momentum-Mamba sequence classifier,
+forward and backward -- 6 MambaMomentum layers, each B=256 sequences, T=300,
+D=512 channels (d_model 256 x expand 2), N=16 states, with the block's
+softplus(delta + bias) and SiLU(z) gate fused into the kernels, fp32.  Metric:
+scan elements (B*T*D*N) per second, fwd+bwd, whole job.  ``--gpus N`` splits
+the 256 sequences over the ranks (B = 256/N each, strong scaling): sequences
+are independent, so the data path has no collective.
+
+Extra keys of the same line (each with its own roofline):
+  * ``stack_cfg1``: the 4-layer stack of d_model 128 (B=32 L=1024 D=256 N=16);
+  * ``long_seq``:   B=8 L=65536 D=2048 N=16 in bf16, split along time over the
+                    ranks (segment summaries all-gathered over NCCL);
+  * ``linoss``:     the LinOSS layer scan, IM and IMEX, B=16 L=4096 P=256;
+  * ``rows``:       the row-form and PScan-layout scans at the stack's size.
+On N > 1 GPUs only ``long_seq`` runs beside the default line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload classifier|stack|long|linoss|rows] [--no-extras]
 
 Rank 0 prints ONE JSON line.  ``--impl reference`` times the CPU restatement
 of the reference algorithm (oracle/, fp32 variant, all host threads) on a
-bounded sample of the same workload.
+bounded sample of the default workload.
 """
 from __future__ import annotations
 
 import argparse
+import datetime
 import json
 import math
 import os
@@ -31,28 +42,21 @@ if ROOT not in sys.path:
 
 METRIC = "scan elements/s (B·L·D·N) fwd+bwd and HBM GB/s vs peak at 1/2/4/8 B200"
 UNIT = "elements/s"
-
-# workload shape
-BSZ, SEQ, DIM, DST, LAYERS = 32, 1024, 256, 16, 4
 BETA, ALPHA = 0.6, 1.0
-ELEMS_PER_LAYER = BSZ * SEQ * DIM * DST
 
-CONFIG = {
-    "workload": "MambaMomentum 4-layer stack scan fwd+bwd (d_model 128, expand 2, d_state 16): "
-                "B=32 L=1024 D=256 N=16 per layer, softplus(delta+bias) and SiLU(z) gate fused",
-    "batch": BSZ, "seqlen": SEQ, "dim": DIM, "dstate": DST, "layers": LAYERS,
-    "beta": BETA, "alpha": ALPHA,
-    "l2": "inputs larger than L2: 4 layers x 138 MB of scan inputs per step",
-}
+# momentum-Mamba sequence classifier: 6 layers of d_model 256, expand 2
+CLASSIFIER = dict(batch=256, seqlen=300, dim=512, dstate=16, layers=6)
+# MambaMomentum stack of d_model 128, expand 2: 4 layers
+STACK1 = dict(batch=32, seqlen=1024, dim=256, dstate=16, layers=4)
 
 
-def fwd_bytes(Bsz=BSZ, L=SEQ, D=DIM, N=DST):
+def fwd_bytes(Bsz, L, D, N):
     """Algorithmic bytes of one forward launch: read x, delta, z, B, C, A, D, bias;
     write out."""
     return 4 * (4 * Bsz * L * D + 2 * Bsz * L * N + D * N + 2 * D)
 
 
-def bwd_bytes(Bsz=BSZ, L=SEQ, D=DIM, N=DST):
+def bwd_bytes(Bsz, L, D, N):
     """Algorithmic bytes of one backward launch: read x, delta, z, dout, B, C, A, D,
     bias; write dx, ddelta, dz, dB, dC, dA, dD, dbias."""
     return 4 * (7 * Bsz * L * D + 4 * Bsz * L * N + 2 * D * N + 4 * D)
@@ -68,12 +72,13 @@ def load_peaks():
         return 6650.0, "fallback"
 
 
-def load_traffic(name="mmscan_bwd_traffic.json"):
-    """DRAM bytes per backward launch (or call) from the committed ncu capture, if any."""
+def load_traffic(name, key=None):
+    """DRAM bytes per launch (or call) from a committed ncu summary, if any."""
     path = os.path.join(ROOT, "profiles", name)
     try:
         with open(path) as f:
-            return json.load(f)
+            d = json.load(f)
+        return d[key] if key else d
     except Exception:
         return None
 
@@ -88,6 +93,10 @@ def max_over_ranks(ms: float, world: int, device=None) -> float:
                      device=device if device is not None else "cpu")
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def ctx_max(ms: float, ctx) -> float:
+    return max_over_ranks(ms, ctx.world, ctx.dev)
 
 
 def job_rate(elems_per_rank: float, world: int, ms_job: float) -> float:
@@ -145,28 +154,115 @@ class ClockSampler:
                 "reasons": sorted(reasons)}
 
 
+class Ctx:
+    """Process-wide state of one benchmark run (one process per GPU)."""
+
+    def __init__(self, args):
+        self.args = args
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dev = None
+
+    def init_gpu(self):
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(self.local)
+        self.dev = torch.device("cuda", self.local)
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                    device_id=self.dev)
+
+    def barrier(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    def close(self):
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+def timed_region(ctx, run, steps):
+    """Barrier + synchronize on both sides, CUDA events around `steps` calls of
+    run() on the current stream, clocks sampled meanwhile on rank 0.  Returns
+    (max-over-ranks ms, clocks)."""
+    import torch
+    sampler = ClockSampler(ctx.local) if (ctx.rank == 0 and not ctx.args.no_clocks) else None
+    if sampler:  # before the barrier, so that every rank starts the timed steps together
+        sampler.start()
+        time.sleep(0.5)
+    ctx.barrier()
+    torch.cuda.synchronize()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ctx.barrier()
+    clocks = sampler.stop() if sampler else None
+    return ctx_max(e0.elapsed_time(e1), ctx), clocks
+
+
+def capture(ctx, fn):
+    """One CUDA graph of fn() (the kernels' shared-memory attributes were set by
+    eager warm-up calls before)."""
+    import torch
+    graph = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream(device=ctx.dev)
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(graph, stream=s):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    graph.replay()
+    torch.cuda.synchronize()
+    return graph
+
+
+def launch_times(pairs, reps=10):
+    """Mean CUDA-event duration of each named launch function, events recorded on
+    the current stream (the stream the library launches on)."""
+    import torch
+    cur = torch.cuda.current_stream()
+    out = {}
+    for name, fn in pairs:
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(reps)]
+        for a, b in evs:
+            a.record(cur)
+            fn()
+            b.record(cur)
+        torch.cuda.synchronize()
+        out[name] = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    return out
+
+
 # ---------------------------------------------------------------------------
-# B200 arm
+# momentum scan stacks (the default classifier line and the d_model-128 stack)
 # ---------------------------------------------------------------------------
 class Layer:
     """Device-resident inputs, outputs and checkpoint workspace of one layer."""
 
-    def __init__(self, torch, lib, dev, gen, Bsz=BSZ):
+    def __init__(self, torch, lib, dev, gen, Bsz, L, D, N):
         f = torch.float32
-        self.Bsz = Bsz
-        self.x = torch.randn(Bsz, SEQ, DIM, device=dev, generator=gen)
-        self.delta = 0.5 * torch.randn(Bsz, SEQ, DIM, device=dev, generator=gen)  # raw dt_proj out
-        self.z = torch.randn(Bsz, SEQ, DIM, device=dev, generator=gen)
-        self.B = torch.randn(Bsz, SEQ, DST, device=dev, generator=gen)
-        self.C = torch.randn(Bsz, SEQ, DST, device=dev, generator=gen)
-        self.A = -torch.arange(1, DST + 1, device=dev, dtype=f).repeat(DIM, 1)
-        self.D = torch.ones(DIM, device=dev)
-        dt = torch.exp(torch.rand(DIM, device=dev, generator=gen) * (math.log(0.1) - math.log(1e-3))
+        self.shape = (Bsz, L, D, N)
+        self.x = torch.randn(Bsz, L, D, device=dev, generator=gen)
+        self.delta = 0.5 * torch.randn(Bsz, L, D, device=dev, generator=gen)  # raw dt_proj out
+        self.z = torch.randn(Bsz, L, D, device=dev, generator=gen)
+        self.B = torch.randn(Bsz, L, N, device=dev, generator=gen)
+        self.C = torch.randn(Bsz, L, N, device=dev, generator=gen)
+        self.A = -torch.arange(1, N + 1, device=dev, dtype=f).repeat(D, 1)
+        self.D = torch.ones(D, device=dev)
+        dt = torch.exp(torch.rand(D, device=dev, generator=gen) * (math.log(0.1) - math.log(1e-3))
                        + math.log(1e-3))
         self.bias = dt + torch.log(-torch.expm1(-dt))          # inverse softplus, as the block
-        self.dout = torch.randn(Bsz, SEQ, DIM, device=dev, generator=gen)
-        self.out = torch.empty(Bsz, SEQ, DIM, device=dev)
-        self.ckpt = torch.empty(lib.mmb_mmscan_ckpt_floats(Bsz, SEQ, DIM, DST), device=dev)
+        self.dout = torch.randn(Bsz, L, D, device=dev, generator=gen)
+        self.out = torch.empty(Bsz, L, D, device=dev)
+        self.ckpt = torch.empty(lib.mmb_mmscan_ckpt_floats(Bsz, L, D, N), device=dev)
         self.dx = torch.empty_like(self.x)
         self.ddelta = torch.empty_like(self.x)
         self.dz = torch.empty_like(self.x)
@@ -177,225 +273,187 @@ class Layer:
         self.dbias = torch.empty_like(self.D)
 
 
-def make_desc(_lib, Bsz):
+def make_desc(_lib, Bsz, L, D, N):
     d = _lib.MMScanDesc()
-    d.batch, d.seqlen, d.dim, d.dstate = Bsz, SEQ, DIM, DST
-    d.x_stride[:] = (SEQ * DIM, DIM)
-    d.delta_stride[:] = (SEQ * DIM, DIM)
-    d.z_stride[:] = (SEQ * DIM, DIM)
-    d.B_stride[:] = (SEQ * DST, DST)
-    d.C_stride[:] = (SEQ * DST, DST)
+    d.batch, d.seqlen, d.dim, d.dstate = Bsz, L, D, N
+    d.x_stride[:] = (L * D, D)
+    d.delta_stride[:] = (L * D, D)
+    d.z_stride[:] = (L * D, D)
+    d.B_stride[:] = (L * N, N)
+    d.C_stride[:] = (L * N, N)
     d.beta, d.alpha, d.delta_softplus = BETA, ALPHA, 1
     return d
 
 
-def run_b200(args):
+def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
+    """Time the scan fwd+bwd of a stack of layers.  strong: the cfg batch is the
+    whole job's, split over the ranks; else every rank runs the whole batch."""
     import torch
-    import torch.distributed as dist
 
     from momentummamba_b200 import _lib
     from momentummamba_b200.selective_scan import selective_scan_momentum_fn
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+    args = ctx.args
+    Btot, L, D, N, NL = (cfg[k] for k in ("batch", "seqlen", "dim", "dstate", "layers"))
+    if strong:
+        if Btot % ctx.world:
+            raise SystemExit(f"batch {Btot} does not split over {ctx.world} ranks")
+        Bsz = Btot // ctx.world
+    else:
+        Bsz = Btot
+    if args.batch:  # profiling of a smaller case of the same kernels
+        Bsz = args.batch
     lib = _lib.load()
-    gen = torch.Generator(device=dev).manual_seed(1234 + rank)
-    bsz = args.batch if args.kernels_only else BSZ
-    layers = [Layer(torch, lib, dev, gen, Bsz=bsz) for _ in range(LAYERS)]
-    desc = make_desc(_lib, bsz)
+    gen = torch.Generator(device=ctx.dev).manual_seed(1234 + ctx.rank)
+    layers = [Layer(torch, lib, ctx.dev, gen, Bsz, L, D, N) for _ in range(NL)]
+    desc = make_desc(_lib, Bsz, L, D, N)
     P = _lib.ptr
 
-    def fwd(ly, stream):
+    def fwd(ly):
         st = lib.mmb_mmscan_fwd(desc, P(ly.x), P(ly.delta), P(ly.A), P(ly.B), P(ly.C), P(ly.D),
-                                P(ly.z), P(ly.bias), P(ly.out), P(ly.ckpt), stream)
+                                P(ly.z), P(ly.bias), P(ly.out), P(ly.ckpt), _lib.stream_of(ly.x))
         _lib.check(st, "fwd")
 
-    def bwd(ly, stream):
+    def bwd(ly):
         st = lib.mmb_mmscan_bwd(desc, P(ly.x), P(ly.delta), P(ly.A), P(ly.B), P(ly.C), P(ly.D),
                                 P(ly.z), P(ly.bias), P(ly.ckpt), P(ly.dout), P(ly.dx),
                                 P(ly.ddelta), P(ly.dA), P(ly.dB), P(ly.dC), P(ly.dD), P(ly.dz),
-                                P(ly.dbias), stream)
+                                P(ly.dbias), _lib.stream_of(ly.x))
         _lib.check(st, "bwd")
 
     def step():
-        s = _lib.stream_of(layers[0].x)
         for ly in layers:
-            fwd(ly, s)
-            bwd(ly, s)
-
-    def barrier():
-        if world > 1:
-            dist.barrier()
+            fwd(ly)
+            bwd(ly)
 
     # warm-up (also sets the kernels' shared-memory attributes before capture)
     for _ in range(max(3, args.warmup)):
         step()
     torch.cuda.synchronize()
-    if args.kernels_only:
-        for _ in range(args.steps):
+    if args.kernels_only:  # eager launches only, for profiler captures
+        for _ in range(steps):
             step()
         torch.cuda.synchronize()
-        if world > 1:
-            dist.destroy_process_group()
         return None
-
-    launch = "eager"
-    graph = None
-    if not args.no_graph:
-        try:
-            graph = torch.cuda.CUDAGraph()
-            s = torch.cuda.Stream(device=dev)
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                with torch.cuda.graph(graph, stream=s):
-                    step()
-            torch.cuda.current_stream().wait_stream(s)
-            graph.replay()
-            torch.cuda.synchronize()
-            launch = "cuda graph"
-        except Exception as e:  # capture unsupported: stay eager, say so
-            graph = None
-            launch = f"eager (graph capture failed: {type(e).__name__})"
-
-    run = graph.replay if graph is not None else step
+    launch = "cuda graph"
+    try:
+        graph = capture(ctx, step)
+        run = graph.replay
+    except Exception as e:  # capture unsupported: stay eager, say so
+        graph = None
+        run = step
+        launch = f"eager (graph capture failed: {type(e).__name__})"
     for _ in range(args.warmup):
         run()
     torch.cuda.synchronize()
+    ms, clocks = timed_region(ctx, run, steps)
+    elems_layer = Bsz * L * D * N
+    value = job_rate(elems_layer * NL * steps, ctx.world, ms)
 
-    sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
-    if sampler:  # before the barrier, so that every rank starts the timed steps together
-        sampler.start()
-        time.sleep(0.5)
-    barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        run()
-    e1.record()
-    torch.cuda.synchronize()
-    barrier()
-    clocks = sampler.stop() if sampler else None
-    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
-    value = job_rate(ELEMS_PER_LAYER * LAYERS * args.steps, world, ms)
+    # per-launch durations of the layer kernels (CUDA events on the launching stream)
+    t = launch_times([("fwd", lambda: fwd(layers[0])), ("bwd", lambda: bwd(layers[1]))], reps=10)
+    t_fwd = ctx_max(t["fwd"], ctx)
+    t_bwd = ctx_max(t["bwd"], ctx)
+    del graph
 
-    # per-kernel durations (CUDA events on the launching stream), for the roofline
-    ly = layers[0]
-    s = _lib.stream_of(ly.x)
-    cs = torch.cuda.current_stream()
-    reps = 20
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(2 * reps)]
-    for i in range(reps):
-        lyr = layers[i % LAYERS]
-        evs[2 * i][0].record(cs)
-        fwd(lyr, s)
-        evs[2 * i][1].record(cs)
-        evs[2 * i + 1][0].record(cs)
-        bwd(lyr, s)
-        evs[2 * i + 1][1].record(cs)
-    torch.cuda.synchronize()
-    t_fwd = statistics.mean(evs[2 * i][0].elapsed_time(evs[2 * i][1]) for i in range(reps))
-    t_bwd = statistics.mean(evs[2 * i + 1][0].elapsed_time(evs[2 * i + 1][1]) for i in range(reps))
-
-    # end to end through the public autograd API with host buffers
-    if world > 1:
-        dist.barrier()
-    e2e = run_e2e(torch, selective_scan_momentum_fn, dev, layers, args)
-    e2e_ms = max_over_ranks(e2e["ms_per_step"], world, dev)
-    e2e["ms_per_step"] = e2e_ms
-    e2e["value"] = job_rate(ELEMS_PER_LAYER * LAYERS, world, e2e_ms)
-
+    e2e = None
+    if with_e2e:
+        ctx.barrier()
+        e2e = run_e2e(torch, selective_scan_momentum_fn, ctx, layers, cfg)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(budget_s=args.cpu_budget)
-
-    if world > 1:
-        dist.destroy_process_group()
-    if rank != 0:
+    if with_cpu and ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
+        cpu = cpu_baseline(cfg, budget_s=args.cpu_budget)
+    del layers
+    torch.cuda.empty_cache()
+    if ctx.rank != 0:
         return None
 
     peak, peak_kind = load_peaks()
-    bwd_b = bwd_bytes()
-    fwd_b = fwd_bytes()
-    achieved = bwd_b / (t_bwd / 1e3) / 1e9
-    traffic = load_traffic()
-    line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": dict(CONFIG, parallelism=f"batch-sharded x{world} (no data-path collective)",
-                       launch=launch),
+    fb, bb = fwd_bytes(Bsz, L, D, N), bwd_bytes(Bsz, L, D, N)
+    achieved = bb / (t_bwd / 1e3) / 1e9
+    traffic = load_traffic("mmscan_bwd_traffic.json", name)
+    workload = (f"{NL}-layer momentum-Mamba scan fwd+bwd (expand 2, d_state {N}): "
+                f"B={Btot} L={L} D={D} N={N} per layer, softplus(delta+bias) and SiLU(z) "
+                f"gate fused, fp32")
+    par = (f"batch split over {ctx.world} rank(s): {Bsz} sequences each, no data-path "
+           f"collective" if strong else f"batch-sharded replicas x{ctx.world}: {Bsz} "
+           f"sequences per rank, no data-path collective")
+    return {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": ctx.world, "steps": steps,
+        "warmup": args.warmup, "ms_per_step": ms / steps, "higher_is_better": True,
+        "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": workload, "batch": Btot, "batch_per_rank": Bsz, "seqlen": L,
+                   "dim": D, "dstate": N, "layers": NL, "beta": BETA, "alpha": ALPHA,
+                   "parallelism": par, "launch": launch,
+                   "l2": f"inputs larger than L2: {NL} layers x "
+                         f"{fwd_bytes(Bsz, L, D, N) / 1e6:.0f} MB of scan inputs per step"},
         "roofline": {
-            "kernel": "mmscan_bwd_kernel<16>", "bound": "hbm", "achieved": achieved,
+            "kernel": f"mmscan_bwd_kernel<{N}>", "bound": "hbm", "achieved": achieved,
             "peak": peak, "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s",
             "frac": achieved / peak,
             "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
-            "algorithmic_bytes": bwd_b, "ms_per_launch": t_bwd,
+            "traffic_note": traffic.get("note") if traffic else None,
+            "algorithmic_bytes": bb, "ms_per_launch": t_bwd,
         },
         "kernels": {
-            "mmscan_fwd_kernel<16>": {"ms": t_fwd, "algorithmic_bytes": fwd_b,
-                                      "GB/s": fwd_b / (t_fwd / 1e3) / 1e9,
-                                      "frac": fwd_b / (t_fwd / 1e3) / 1e9 / peak},
-            "mmscan_bwd_kernel<16>": {"ms": t_bwd, "algorithmic_bytes": bwd_b,
-                                      "GB/s": achieved, "frac": achieved / peak},
+            f"mmscan_fwd_kernel<{N}>": {"ms": t_fwd, "algorithmic_bytes": fb,
+                                        "GB/s": fb / (t_fwd / 1e3) / 1e9,
+                                        "frac": fb / (t_fwd / 1e3) / 1e9 / peak},
+            f"mmscan_bwd_kernel<{N}>": {"ms": t_bwd, "algorithmic_bytes": bb,
+                                        "GB/s": achieved, "frac": achieved / peak},
         },
-        "hbm_gbs_step": LAYERS * (fwd_b + bwd_b) * args.steps / (ms / 1e3) / 1e9,
+        "hbm_gbs_step": NL * (fb + bb) * steps / (ms / 1e3) / 1e9,
         "e2e": e2e,
-        "gpu_launches": 3 * LAYERS * args.steps,  # per layer: forward, clearing of the sums, backward
+        # per layer: forward, clearing of the backward's sums, backward
+        "gpu_launches": 3 * NL * steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
-    return line
 
 
-def run_e2e(torch, fn, dev, layers, args, steps=8):
+def run_e2e(torch, fn, ctx, layers, cfg, steps=4):
     """Same metric through selective_scan_momentum_fn + autograd, with each
     layer's inputs copied in from pinned host memory and all its outputs copied
     back every step.  The copies run on two side streams so that the next
     layer's inputs come in while the previous layer's outputs go out (PCIe is
     full duplex), and a step's uploads may start while the previous step's
     outputs still go out (steady state of a stream of batches); the scans run on
-    the current stream in layer order.  The timed region ends after the last
-    step's outputs reached the host."""
-    host_in, host_out = [], []
-    for ly in layers:
-        host_in.append({k: getattr(ly, k).cpu().pin_memory()
-                        for k in ("x", "delta", "z", "B", "C", "dout")})
-        host_out.append({k: torch.empty(getattr(ly, k).shape, pin_memory=True)
-                         for k in ("out", "dx", "ddelta", "dz", "dB", "dC", "dA", "dD", "dbias")})
-    A, D, bias = layers[0].A, layers[0].D, layers[0].bias
-    h2d = sum(t.numel() * 4 for t in host_in[0].values()) * LAYERS
-    d2h = sum(t.numel() * 4 for t in host_out[0].values()) * LAYERS
+    the current stream in layer order.  Every layer reads the same pinned host
+    inputs and writes the same pinned host outputs (one set of host buffers).
+    The timed region ends after the last step's outputs reached the host."""
+    dev = ctx.dev
+    NL = len(layers)
+    ly0 = layers[0]
+    host_in = {k: getattr(ly0, k).cpu().pin_memory()
+               for k in ("x", "delta", "z", "B", "C", "dout")}
+    host_out = {k: torch.empty(getattr(ly0, k).shape, pin_memory=True)
+                for k in ("out", "dx", "ddelta", "dz", "dB", "dC", "dA", "dD", "dbias")}
+    A, D, bias = ly0.A, ly0.D, ly0.bias
+    h2d = sum(t.numel() * 4 for t in host_in.values()) * NL
+    d2h = sum(t.numel() * 4 for t in host_out.values()) * NL
     comp = torch.cuda.current_stream(dev)
     s_in = torch.cuda.Stream(device=dev)
     s_out = torch.cuda.Stream(device=dev)
+    Bsz, L, Dm, N = ly0.shape
 
     def one():
-        dev_in = [None] * LAYERS
+        dev_in = [None] * NL
 
         def fetch(i):
             with torch.cuda.stream(s_in):
-                dev_in[i] = {k: v.to(dev, non_blocking=True) for k, v in host_in[i].items()}
+                dev_in[i] = {k: v.to(dev, non_blocking=True) for k, v in host_in.items()}
                 ev = torch.cuda.Event()
                 ev.record(s_in)
             return ev
 
         ready = fetch(0)
-        for i in range(LAYERS):
+        for i in range(NL):
             comp.wait_event(ready)
             d = dev_in[i]
             for t in d.values():
                 t.record_stream(comp)
-            if i + 1 < LAYERS:
+            if i + 1 < NL:
                 ready = fetch(i + 1)
             ins = [d["x"].requires_grad_(True), d["delta"].requires_grad_(True),
                    A.detach().requires_grad_(True), d["B"].requires_grad_(True),
@@ -413,10 +471,11 @@ def run_e2e(torch, fn, dev, layers, args, steps=8):
                 for k, v in outs:
                     v = v.detach()
                     v.record_stream(s_out)
-                    host_out[i][k].copy_(v, non_blocking=True)
+                    host_out[k].copy_(v, non_blocking=True)
 
     one()
     torch.cuda.synchronize()
+    ctx.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     e0.record(comp)
@@ -427,10 +486,13 @@ def run_e2e(torch, fn, dev, layers, args, steps=8):
     comp.wait_stream(s_out)
     e1.record(comp)
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
-    return {"value": ELEMS_PER_LAYER * LAYERS / (ms / 1e3), "unit": UNIT,
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": ms,
-            "steps": steps, "api": "selective_scan_momentum_fn + torch.autograd.grad",
+    ms = ctx_max(e0.elapsed_time(e1) / steps, ctx)
+    elems = Bsz * L * Dm * N * NL
+    return {"value": job_rate(elems, ctx.world, ms), "unit": UNIT,
+            "h2d_bytes_per_step": h2d * ctx.world, "d2h_bytes_per_step": d2h * ctx.world,
+            "h2d_bytes_per_rank_step": h2d, "d2h_bytes_per_rank_step": d2h,
+            "ms_per_step": ms, "steps": steps,
+            "api": "selective_scan_momentum_fn + torch.autograd.grad",
             "copies": "pinned host buffers; inputs of layer i+1 (and of the next step) in "
                       "while outputs of layer i go out (two copy streams)"}
 
@@ -438,20 +500,21 @@ def run_e2e(torch, fn, dev, layers, args, steps=8):
 # ---------------------------------------------------------------------------
 # CPU (oracle restatement of the reference algorithm)
 # ---------------------------------------------------------------------------
-def cpu_inputs(np, nseq, seed=0):
+def cpu_inputs(np, cfg, nseq, seed=0):
+    L, D, N = cfg["seqlen"], cfg["dim"], cfg["dstate"]
     rng = np.random.default_rng(seed)
     f = np.float32
-    x = rng.standard_normal((nseq, SEQ, DIM), dtype=f)
-    delta = (0.5 * rng.standard_normal((nseq, SEQ, DIM))).astype(f)
-    z = rng.standard_normal((nseq, SEQ, DIM), dtype=f)
-    B = rng.standard_normal((nseq, SEQ, DST), dtype=f)
-    C = rng.standard_normal((nseq, SEQ, DST), dtype=f)
-    A = -np.tile(np.arange(1, DST + 1, dtype=f), (DIM, 1))
-    D = np.ones(DIM, f)
-    dt = np.exp(rng.uniform(math.log(1e-3), math.log(0.1), DIM))
+    x = rng.standard_normal((nseq, L, D), dtype=f)
+    delta = (0.5 * rng.standard_normal((nseq, L, D))).astype(f)
+    z = rng.standard_normal((nseq, L, D), dtype=f)
+    B = rng.standard_normal((nseq, L, N), dtype=f)
+    C = rng.standard_normal((nseq, L, N), dtype=f)
+    A = -np.tile(np.arange(1, N + 1, dtype=f), (D, 1))
+    Dv = np.ones(D, f)
+    dt = np.exp(rng.uniform(math.log(1e-3), math.log(0.1), D))
     bias = (dt + np.log(-np.expm1(-dt))).astype(f)
-    dout = rng.standard_normal((nseq, SEQ, DIM), dtype=f)
-    return x, delta, A, B, C, D, z, bias, dout
+    dout = rng.standard_normal((nseq, L, D), dtype=f)
+    return x, delta, A, B, C, Dv, z, bias, dout
 
 
 def cpu_scan_layer(oracle, inp):
@@ -467,16 +530,17 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def cpu_baseline(budget_s=15.0):
+def cpu_baseline(cfg, budget_s=15.0, nseq=None):
     """Time the fp32 oracle (the reference recurrence restated in C) on the host
-    cores: whole layers of 4 sequences each, repeated until ~budget_s."""
+    cores: whole layers of a few sequences each, repeated until ~budget_s."""
     import numpy as np
 
     import oracle
     cores = cpu_threads()
     oracle.set_num_threads(cores)
-    nseq = 4
-    inp = cpu_inputs(np, nseq)
+    L, D, N = cfg["seqlen"], cfg["dim"], cfg["dstate"]
+    nseq = nseq or max(1, min(cfg["batch"], int(round(2e7 / (L * D * N)))))
+    inp = cpu_inputs(np, cfg, nseq)
     cpu_scan_layer(oracle, inp)  # warm
     t0 = time.perf_counter()
     n = 0
@@ -486,13 +550,16 @@ def cpu_baseline(budget_s=15.0):
         if time.perf_counter() - t0 >= budget_s:
             break
     dt = time.perf_counter() - t0
-    elems = n * nseq * SEQ * DIM * DST
+    elems = n * nseq * L * D * N
     return {"value": elems / dt, "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{n} layer passes (fwd+bwd) of {nseq} of the {BSZ} sequences, "
-                      f"{dt:.1f} s of CPU time; fp32 oracle/scan_oracle.c, OpenMP"}
+            "sample": f"{n} layer passes (fwd+bwd) of {nseq} of the {cfg['batch']} sequences "
+                      f"(L={L} D={D} N={N}), {dt:.1f} s of CPU time; fp32 oracle/scan_oracle.c, "
+                      f"OpenMP"}
 
 
 def run_reference(args):
+    """The reference arm: the CPU restatement of the reference recurrence on the
+    host cores, on the default workload's shapes (rank 0 only)."""
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
@@ -500,32 +567,39 @@ def run_reference(args):
     import numpy as np
 
     import oracle
+    cfg = CLASSIFIER
+    L, D, N = cfg["seqlen"], cfg["dim"], cfg["dstate"]
     cores = cpu_threads()
     oracle.set_num_threads(cores)
     # size each step so that warm-up + steps take about a minute
-    probe = cpu_inputs(np, 1)
+    probe = cpu_inputs(np, cfg, 4)
     t0 = time.perf_counter()
     cpu_scan_layer(oracle, probe)
-    t_seq = time.perf_counter() - t0
+    t_seq = (time.perf_counter() - t0) / 4
     total = max(1, args.steps + args.warmup)
-    nseq = int(max(1, min(BSZ, round(60.0 / (total * max(t_seq, 1e-3))))))
-    inp = cpu_inputs(np, nseq)
+    nseq = int(max(1, min(cfg["batch"], round(60.0 / (total * max(t_seq, 1e-4))))))
+    inp = cpu_inputs(np, cfg, nseq)
     for _ in range(args.warmup):
         cpu_scan_layer(oracle, inp)
     t0 = time.perf_counter()
     for _ in range(args.steps):
         cpu_scan_layer(oracle, inp)
     dt = time.perf_counter() - t0
-    elems = args.steps * nseq * SEQ * DIM * DST
+    elems = args.steps * nseq * L * D * N
     value = elems / dt
-    sample = (f"each step: one layer's scan fwd+bwd on {nseq} of the {BSZ} sequences "
-              f"({nseq * SEQ * DIM * DST} elements); fp32 oracle/scan_oracle.c, OpenMP")
+    sample = (f"each step: one layer's scan fwd+bwd on {nseq} of the {cfg['batch']} sequences "
+              f"({nseq * L * D * N} elements); fp32 oracle/scan_oracle.c, OpenMP")
+    workload = (f"{cfg['layers']}-layer momentum-Mamba scan fwd+bwd (expand 2, d_state {N}): "
+                f"B={cfg['batch']} L={L} D={D} N={N} per layer, softplus(delta+bias) and SiLU(z) "
+                f"gate fused, fp32")
     return {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": dt * 1e3 / max(1, args.steps),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "impl": "reference",
-        "config": dict(CONFIG, parallelism="host cores (rank 0 only)"),
+        "config": {"workload": workload, "batch": cfg["batch"], "seqlen": L, "dim": D,
+                   "dstate": N, "layers": cfg["layers"], "beta": BETA, "alpha": ALPHA,
+                   "parallelism": "host cores (rank 0 only)"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -547,26 +621,19 @@ def long_bytes(Bsz, L, D, N):
     return fwd, bwd
 
 
-def run_long(args):
+def run_long(ctx, steps):
     """B=8, L=65536, D=2048, N=16 with bf16 activations, fp32 state: the
     sequence is split into WORLD_SIZE contiguous segments, one per rank
     (segment summaries all-gathered over NCCL, carries folded locally).  Total
     work is fixed (strong scaling)."""
-    import datetime
-
     import torch
     import torch.distributed as dist
 
     from momentummamba_b200.selective_scan import ScanCall
     from momentummamba_b200.seqshard import SegmentOps as ops
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    args = ctx.args
+    world, rank, dev = ctx.world, ctx.rank, ctx.dev
     Bsz, L, D, N = (LONG[k] for k in ("batch", "seqlen", "dim", "dstate"))
     beta, alpha = LONG["beta"], LONG["alpha"]
     Lr = L // world
@@ -623,43 +690,26 @@ def run_long(args):
         step()
     torch.cuda.synchronize()
     marks.clear()
-    sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
-    if sampler:  # before the barrier, so that every rank starts the timed steps together
-        sampler.start()
-        time.sleep(0.5)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        step()
-    e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop() if sampler else None
-    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
+    ms, clocks = timed_region(ctx, step, steps)
     phases = None
     if args.phases and marks:
         names = ["start", "fwd_carry", "fwd", "bwd_carry", "bwd"]
         phases = {}
         for a, b in zip(names[:-1], names[1:]):
-            t = statistics.mean(marks[a][i].elapsed_time(marks[b][i]) for i in range(args.steps))
-            phases[b] = max_over_ranks(t, world, dev)
-    if world > 1:
-        dist.destroy_process_group()
+            t = statistics.mean(marks[a][i].elapsed_time(marks[b][i]) for i in range(steps))
+            phases[b] = ctx_max(t, ctx)
+    del x, delta, Bm, Cm, dout, call
+    torch.cuda.empty_cache()
     if rank != 0:
         return None
     elems = Bsz * L * D * N
     fb, bb = long_bytes(Bsz, Lr, D, N)
     peak, peak_kind = load_peaks()
-    ms_step = ms / args.steps
+    ms_step = ms / steps
     achieved = (fb + bb) / (ms_step / 1e3) / 1e9  # per GPU: its segment's bytes over the step
     return {
         "metric": METRIC, "value": elems / (ms_step / 1e3), "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+        "steps": steps, "warmup": args.warmup, "ms_per_step": ms_step,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic",
         "config": {"workload": "long-sequence scan fwd+bwd: B=8 L=65536 D=2048 N=16, bf16 "
@@ -674,7 +724,7 @@ def run_long(args):
         "phases_ms": phases,
         # rank 0: forward, clearing of the backward's sums, backward; with segments also
         # both summaries and the adjoint fold
-        "gpu_launches": (3 if world == 1 else 6) * args.steps,
+        "gpu_launches": (3 if world == 1 else 6) * steps,
         "clocks": clocks,
     }
 
@@ -685,29 +735,20 @@ def run_long(args):
 LINOSS = dict(batch=16, seqlen=4096, osc=256)
 
 
-def run_linoss(args):
+def run_linoss(ctx, steps):
     """The LinOSS layer scan (LinOSS_pytorch.py:153-239, time-invariant 2x2
     transition built in-kernel) forward + backward for IM and IMEX at B=16
     L=4096 P=256 with complex Bu ~ N(0,1), A ~ U[0,1], step = exp(U[ln 1e-3,
     ln 1e-1]).  One step = IM fwd + bwd and IMEX fwd + bwd; elements = B L P
     oscillator steps per discretisation.  Batch-sharded over ranks (weak)."""
-    import datetime
-
     import torch
-    import torch.distributed as dist
 
     from momentummamba_b200 import _lib
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    args, dev, world = ctx.args, ctx.dev, ctx.world
     lib = _lib.load()
     Bsz, L, P = LINOSS["batch"], LINOSS["seqlen"], LINOSS["osc"]
-    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    g = torch.Generator(device=dev).manual_seed(5 + ctx.rank)
     A = torch.rand(P, device=dev, generator=g)
     step = torch.exp(torch.rand(P, device=dev, generator=g) * (math.log(0.1) - math.log(1e-3))
                      + math.log(1e-3))
@@ -737,52 +778,16 @@ def run_linoss(args):
     for _ in range(max(3, args.warmup)):
         stepfn()
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    cs = torch.cuda.Stream(device=dev)
-    cs.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(cs):
-        with torch.cuda.graph(graph, stream=cs):
-            stepfn()
-    torch.cuda.current_stream().wait_stream(cs)
+    graph = capture(ctx, stepfn)
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.5)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop() if sampler else None
-    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
-    # per-kernel durations
-    reps = 10
-    t = {}
-    cur = torch.cuda.current_stream()
-    for name, fn in (("fwd_IM", lambda: fwd(0)), ("bwd_IM", lambda: bwd(0)),
-                     ("fwd_IMEX", lambda: fwd(1)), ("bwd_IMEX", lambda: bwd(1))):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(reps)]
-        for a, b in evs:
-            a.record(cur)
-            fn()
-            b.record(cur)
-        torch.cuda.synchronize()
-        t[name] = statistics.mean(a.elapsed_time(b) for a, b in evs)
-    del graph
-    if world > 1:
-        dist.destroy_process_group()
-    if rank != 0:
+    ms, clocks = timed_region(ctx, graph.replay, steps)
+    t = launch_times((("fwd_IM", lambda: fwd(0)), ("bwd_IM", lambda: bwd(0)),
+                      ("fwd_IMEX", lambda: fwd(1)), ("bwd_IMEX", lambda: bwd(1))))
+    del graph, Bu, dx2, x2, dBu, works
+    torch.cuda.empty_cache()
+    if ctx.rank != 0:
         return None
     elems = Bsz * L * P
     fwd_b = elems * 16 + 2 * P * 4          # read Bu, write x2 (complex fp32)
@@ -790,10 +795,13 @@ def run_linoss(args):
     peak, peak_kind = load_peaks()
     achieved = bwd_b / (t["bwd_IM"] / 1e3) / 1e9
     tr = load_traffic("linoss_bwd_traffic.json")
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cpu = linoss_cpu_baseline(budget_s=min(5.0, args.cpu_budget))
     return {
-        "metric": METRIC, "value": job_rate(2 * elems * args.steps, world, ms), "unit": UNIT,
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": job_rate(2 * elems * steps, world, ms), "unit": UNIT,
+        "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "LinOSS layer scan fwd+bwd, IM and IMEX: B=16 L=4096 P=256, "
                                "complex Bu ~ N(0,1), A ~ U[0,1], step = exp(U[ln 1e-3, ln 1e-1]); "
@@ -810,43 +818,69 @@ def run_linoss(args):
                     for k, v in t.items()},
         # per discretisation: forward summary, carry, final; backward summary, carry,
         # final, parameter chain rule
-        "gpu_launches": 14 * args.steps,
+        "gpu_launches": 14 * steps,
         "clocks": clocks,
+        "cpu_baseline": cpu,
     }
+
+
+def linoss_cpu_baseline(budget_s=5.0):
+    """The fp32 oracle's 2x2 scan (forward + backward) on the host cores, for one
+    sequence of the LinOSS workload (IM transition)."""
+    import numpy as np
+
+    import oracle
+    cores = cpu_threads()
+    oracle.set_num_threads(cores)
+    L, P = LINOSS["seqlen"], LINOSS["osc"]
+    rng = np.random.default_rng(0)
+    Ad = rng.uniform(0, 1, P)
+    st = np.exp(rng.uniform(math.log(1e-3), math.log(0.1), P))
+    S = 1.0 / (1.0 + st ** 2 * Ad)
+    M = np.broadcast_to(np.concatenate([1.0 - st ** 2 * Ad * S, -st * Ad * S, st * S, S]),
+                        (1, L, 4 * P)).astype(np.float32)
+    Fc = (rng.standard_normal((1, L, 2 * P)) + 1j * rng.standard_normal((1, L, 2 * P))).astype(
+        np.complex64)
+    gX = (rng.standard_normal((1, L, 2 * P)) + 1j * rng.standard_normal((1, L, 2 * P))).astype(
+        np.complex64)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        Ms, X = oracle.scan2_fwd(M, Fc, prec="f32")
+        oracle.scan2_bwd(M, X, gX, prec="f32")
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": n * L * P / dt, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{n} fwd+bwd passes of the generic 2x2 scan over 1 of the 16 sequences "
+                      f"(L={L}, P={P}, complex F), {dt:.1f} s; fp32 oracle/scan_oracle.c"}
 
 
 # ---------------------------------------------------------------------------
 # row-form and PScan-layout scans (the reference's materialised-tensor paths)
 # ---------------------------------------------------------------------------
-def run_rows(args):
+def run_rows(ctx, steps):
     """The momentum row scan (momentum_scan_cuda.py:204-253: R = B*D*N rows of L
     steps) and the diagonal scan in the PScan layout (pscan.py:43-234: (B, L,
-    D*N)) forward + backward at the stack's size (B=32, L=1024, D=256, N=16:
-    134,217,728 elements each).  One step = rows fwd + bwd, then pscan fwd + bwd;
-    elements = the rows scan's (the line's value), per-kernel GB/s for both.
-    Batch-sharded replicas over ranks (weak)."""
-    import datetime
-
+    D*N)) forward + backward at the d_model-128 stack's size (B=32, L=1024,
+    D=256, N=16: 134,217,728 elements each).  One step = rows fwd + bwd, then
+    pscan fwd + bwd; elements = the rows scan's (the line's value), per-kernel
+    GB/s for both.  Batch-sharded replicas over ranks (weak)."""
     import torch
-    import torch.distributed as dist
 
     from momentummamba_b200 import _lib
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    args, dev, world = ctx.args, ctx.dev, ctx.world
     lib = _lib.load()
-    R, L, M = BSZ * DIM * DST, SEQ, DIM * DST
-    g = torch.Generator(device=dev).manual_seed(7 + rank)
+    BS, L, D, N = STACK1["batch"], STACK1["seqlen"], STACK1["dim"], STACK1["dstate"]
+    R, M = BS * D * N, D * N
+    g = torch.Generator(device=dev).manual_seed(7 + ctx.rank)
     a = torch.exp(-torch.rand(R, L, device=dev, generator=g) * 0.2)     # decay factors in (0.82, 1]
     u = torch.randn(R, L, device=dev, generator=g)
     gr = torch.randn(R, L, device=dev, generator=g)
     h, da, du = torch.empty_like(a), torch.empty_like(a), torch.empty_like(a)
-    A3, X3, G3 = a.view(BSZ, L, M), u.view(BSZ, L, M), gr.view(BSZ, L, M)  # same bytes, PScan layout
+    A3, X3, G3 = a.view(BS, L, M), u.view(BS, L, M), gr.view(BS, L, M)  # same bytes, PScan layout
     H3, dA3, dX3 = torch.empty_like(A3), torch.empty_like(A3), torch.empty_like(A3)
     Pp = _lib.ptr
 
@@ -859,11 +893,11 @@ def run_rows(args):
                                     _lib.stream_of(a)), "rows bwd")
 
     def ps_fwd():
-        _lib.check(lib.mmb_pscan_fwd(BSZ, L, M, Pp(A3), Pp(X3), Pp(H3), _lib.stream_of(a)),
+        _lib.check(lib.mmb_pscan_fwd(BS, L, M, Pp(A3), Pp(X3), Pp(H3), _lib.stream_of(a)),
                    "pscan fwd")
 
     def ps_bwd():
-        _lib.check(lib.mmb_pscan_bwd(BSZ, L, M, Pp(A3), Pp(H3), Pp(G3), Pp(dA3), Pp(dX3),
+        _lib.check(lib.mmb_pscan_bwd(BS, L, M, Pp(A3), Pp(H3), Pp(G3), Pp(dA3), Pp(dX3),
                                      _lib.stream_of(a)), "pscan bwd")
 
     def stepfn():
@@ -875,51 +909,16 @@ def run_rows(args):
     for _ in range(max(3, args.warmup)):
         stepfn()
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    cs = torch.cuda.Stream(device=dev)
-    cs.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(cs):
-        with torch.cuda.graph(graph, stream=cs):
-            stepfn()
-    torch.cuda.current_stream().wait_stream(cs)
+    graph = capture(ctx, stepfn)
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
-    sampler = ClockSampler(local) if (rank == 0 and not args.no_clocks) else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.5)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize()
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        graph.replay()
-    e1.record()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    clocks = sampler.stop() if sampler else None
-    ms = max_over_ranks(e0.elapsed_time(e1), world, dev)
-    reps = 10
-    t = {}
-    cur = torch.cuda.current_stream()
-    for name, fn in (("rows_fwd", rows_fwd), ("rows_bwd", rows_bwd), ("pscan_fwd", ps_fwd),
-                     ("pscan_bwd", ps_bwd)):
-        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(reps)]
-        for e_a, e_b in evs:
-            e_a.record(cur)
-            fn()
-            e_b.record(cur)
-        torch.cuda.synchronize()
-        t[name] = statistics.mean(x.elapsed_time(y) for x, y in evs)
-    del graph
-    if world > 1:
-        dist.destroy_process_group()
-    if rank != 0:
+    ms, clocks = timed_region(ctx, graph.replay, steps)
+    t = launch_times((("rows_fwd", rows_fwd), ("rows_bwd", rows_bwd), ("pscan_fwd", ps_fwd),
+                      ("pscan_bwd", ps_bwd)))
+    del graph, a, u, gr, h, da, du, H3, dA3, dX3
+    torch.cuda.empty_cache()
+    if ctx.rank != 0:
         return None
     elems = R * L
     nbytes = {"rows_fwd": 12 * elems, "rows_bwd": 20 * elems,   # a, u -> h; g, a, h -> da, du
@@ -928,14 +927,14 @@ def run_rows(args):
     kern = {k: {"ms": v, "algorithmic_bytes": nbytes[k], "GB/s": nbytes[k] / (v / 1e3) / 1e9,
                 "frac": nbytes[k] / (v / 1e3) / 1e9 / peak} for k, v in t.items()}
     return {
-        "metric": METRIC, "value": job_rate(elems * args.steps, world, ms), "unit": UNIT,
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": ms / args.steps, "higher_is_better": True, "scaling": "weak",
+        "metric": METRIC, "value": job_rate(elems * steps, world, ms), "unit": UNIT,
+        "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "materialised-tensor scans at the stack's size: momentum row scan "
-                               "(R=131072 rows x L=1024, beta 0.6) and PScan-layout diagonal scan "
-                               "(B=32 L=1024 M=4096), fwd+bwd each; value = row-scan elements/s "
-                               "over the whole step",
+        "config": {"workload": "materialised-tensor scans at the d_model-128 stack's size: "
+                               "momentum row scan (R=131072 rows x L=1024, beta 0.6) and "
+                               "PScan-layout diagonal scan (B=32 L=1024 M=4096), fwd+bwd each; "
+                               "value = row-scan elements/s over the whole step",
                    "parallelism": f"batch-sharded x{world}", "launch": "cuda graph",
                    "l2": "inputs larger than L2 (537 MB per tensor)"},
         "roofline": {"kernel": "rows_bwd", "bound": "hbm", "achieved": kern["rows_bwd"]["GB/s"],
@@ -943,44 +942,83 @@ def run_rows(args):
                      "frac": kern["rows_bwd"]["frac"], "algorithmic_bytes": nbytes["rows_bwd"],
                      "ms_per_launch": t["rows_bwd"], "traffic": None},
         "kernels": kern,
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": 4 * steps,
         "clocks": clocks,
     }
+
+
+def summary(line):
+    """The part of a workload's line kept as an extra key of the default line."""
+    if line is None:
+        return None
+    keep = ("value", "unit", "n_gpus", "steps", "ms_per_step", "scaling", "dtype", "config",
+            "roofline", "kernels", "phases_ms", "gpu_launches", "clocks", "cpu_baseline")
+    return {k: line[k] for k in keep if k in line}
 
 
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=1000)
+    ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
-    ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="default workload only (no extra keys)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--workload", choices=["classifier", "stack", "long", "linoss", "rows"],
+                    default="classifier",
+                    help="classifier: the 6-layer momentum-Mamba classifier scan, B=256 T=300 "
+                         "D=512 split over the ranks (the benchmark line, with the other "
+                         "workloads as extra keys); stack: the 4-layer d_model-128 stack, "
+                         "B=32 L=1024 D=256 per rank; long: B=8 L=65536 D=2048 bf16, "
+                         "sequence-sharded; linoss: the LinOSS layer scan, IM and IMEX, "
+                         "B=16 L=4096 P=256; rows: the row-form and PScan-layout scans")
     ap.add_argument("--kernels-only", action="store_true",
-                    help="run warm-up and steps eagerly and exit (for profiler captures)")
-    ap.add_argument("--batch", type=int, default=BSZ,
-                    help="sequences per layer (profiling only; the benchmark line uses 32)")
-    ap.add_argument("--workload", choices=["stack", "long", "linoss", "rows"], default="stack",
-                    help="stack: the 4-layer MambaMomentum scan (batch-sharded, the benchmark "
-                         "line); long: B=8 L=65536 D=2048 bf16, sequence-sharded; linoss: the "
-                         "LinOSS layer scan, IM and IMEX, B=16 L=4096 P=256; rows: the "
-                         "row-form and PScan-layout scans at the stack's size")
+                    help="classifier/stack: warm-up and steps as eager launches, nothing "
+                         "else (for profiler captures)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="classifier/stack: sequences per rank (profiling of a smaller case "
+                         "only; the benchmark line uses the configuration's batch)")
     ap.add_argument("--phases", action="store_true",
                     help="long workload: also time each phase (adds events to the step)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":
         line = run_reference(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+    ctx = Ctx(args)
+    ctx.init_gpu()
+    K = args.steps
+    if args.workload == "classifier":
+        line = run_stack(ctx, CLASSIFIER, True, K, with_e2e=True, with_cpu=True,
+                         name="classifier")
+        if not args.no_extras and not args.kernels_only:
+            extras = {}
+            if ctx.world == 1:
+                extras["stack_cfg1"] = summary(run_stack(ctx, STACK1, False, 4 * K,
+                                                         with_e2e=False, with_cpu=True,
+                                                         name="stack_cfg1"))
+            extras["long_seq"] = summary(run_long(ctx, max(3, K // 40)))
+            if ctx.world == 1:
+                extras["linoss"] = summary(run_linoss(ctx, 2 * K))
+                extras["rows"] = summary(run_rows(ctx, max(3, K // 4)))
+            if line is not None:
+                line["extras"] = extras
+                line["gpu_launches_extras"] = sum(
+                    (v or {}).get("gpu_launches", 0) for v in extras.values())
+    elif args.workload == "stack":
+        line = run_stack(ctx, STACK1, False, K, with_e2e=True, with_cpu=True, name="stack_cfg1")
     elif args.workload == "long":
-        line = run_long(args)
+        line = run_long(ctx, K)
     elif args.workload == "linoss":
-        line = run_linoss(args)
-    elif args.workload == "rows":
-        line = run_rows(args)
+        line = run_linoss(ctx, K)
     else:
-        line = run_b200(args)
+        line = run_rows(ctx, K)
+    ctx.close()
     if line is not None:
         print(json.dumps(line), flush=True)
 

@@ -53,6 +53,15 @@ const char* mmb_last_error(void);
  * wait on transaction barriers with an iteration limit.  MMB_OK otherwise. */
 int mmb_device_status(mmb_stream_t stream);
 
+/* Self-test of that error path (no reference counterpart: the reference checks
+ * no device-side error at all, momentum_scan_cuda.py:107,132 only synchronise).
+ * Launches one CTA on `stream` that arms a transaction barrier for bytes that
+ * never arrive (it issues no copy, so nothing asynchronous is left behind),
+ * waits on it with at most `polls` polls (1..4096, else MMB_ERR_SHAPE), gives
+ * up and sets the device flag: the next mmb_device_status then returns
+ * MMB_ERR_TIMEOUT and clears it.  The GPU context stays usable. */
+int mmb_selftest_device_wait(int32_t polls, mmb_stream_t stream);
+
 /* =========================================================================
  * Momentum selective scan (fused discretisation, scan, C-contraction, D skip,
  * optional softplus(delta + bias) and optional SiLU(z) gate):
@@ -340,7 +349,9 @@ int mmb_scan2_bwd(int64_t batch, int64_t L, int64_t P, int32_t complex_f, const 
  * mmb_scan2_fwd would use does not fit, fewer, longer chunks are used, so
  * results agree with mmb_scan2_fwd to rounding.
  * The first call on each device looks up the array's device address; make
- * that first call before any stream capture on that device.  All calls on a
+ * that first call before any stream capture on that device.  The address is
+ * kept until the process exits: calls after a cudaDeviceReset of that device
+ * in the same process are not supported.  All calls on a
  * device share the one array and it keeps the last call's contents (nothing in
  * it needs to start at zero): calls that can overlap on the GPU race, so the
  * caller must order them, e.g. on one stream.

@@ -66,6 +66,7 @@ _SIGNATURES = {
     "mmb_abi_version": (ctypes.c_int, []),
     "mmb_last_error": (ctypes.c_char_p, []),
     "mmb_device_status": (ctypes.c_int, [_c_p]),
+    "mmb_selftest_device_wait": (ctypes.c_int, [_c_i32, _c_p]),
     "mmb_mmscan_ckpt_floats": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
     "mmb_mmscan_fwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 10 + [_c_p]),
     "mmb_mmscan_bwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 18 + [_c_p]),

@@ -51,6 +51,7 @@ int* mmb_device_error_flag() {
 }
 
 extern "C" int mmb_device_status(mmb_stream_t stream) {
+    MMB_NVTX("mmb_device_status");
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     cudaError_t e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) {
@@ -69,6 +70,33 @@ extern "C" int mmb_device_status(mmb_stream_t stream) {
         return MMB_ERR_TIMEOUT;
     }
     return MMB_OK;
+}
+
+// Self-test of the device error path.  One CTA arms an mbarrier for 16 bytes
+// of a transaction that never comes -- no copy is issued, so nothing
+// asynchronous is outstanding when the CTA leaves -- and waits on it the way the
+// tile pipelines do, with at most `polls` polls.  The wait gives up, the CTA
+// sets the device error flag (as a pipeline that gave up does) and returns.
+__global__ void selftest_wait_kernel(int polls, int* err) {
+    __shared__ uint64_t bar;
+    if (threadIdx.x == 0) {
+        mmb::mbar_init(&bar, 1);
+        mmb::mbar_fence_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) mmb::mbar_expect_tx(&bar, 16);
+    __syncthreads();
+    const bool landed = mmb::mbar_wait_polls(&bar, 0, polls);
+    if (__syncthreads_or(!landed) && threadIdx.x == 0 && err) atomicOr(err, 1);
+}
+
+extern "C" int mmb_selftest_device_wait(int32_t polls, mmb_stream_t stream) {
+    MMB_NVTX("mmb_selftest_device_wait");
+    if (polls < 1 || polls > 4096) return MMB_ERR_SHAPE;
+    int* err = mmb_device_error_flag();
+    if (!err) return MMB_ERR_LAUNCH;
+    selftest_wait_kernel<<<1, 32, 0, reinterpret_cast<cudaStream_t>(stream)>>>(polls, err);
+    return mmb_launch_status();
 }
 
 // ---------------------------------------------------------------------------

@@ -270,6 +270,7 @@ extern "C" int mmb_conv1d_silu_fwd(int64_t batch, int64_t seqlen, int64_t dim, i
                                    const float* x, const int64_t* x_stride, const float* weight,
                                    const float* bias, const float* state_in, float* state_out,
                                    float* out, mmb_stream_t stream) {
+    MMB_NVTX("mmb_conv1d_silu_fwd");
     ConvParams p;
     int st = conv_fill(batch, seqlen, dim, width, x, x_stride, weight, bias, p);
     if (st != MMB_OK) return st;
@@ -284,6 +285,7 @@ extern "C" int mmb_conv1d_silu_bwd(int64_t batch, int64_t seqlen, int64_t dim, i
                                    const float* x, const int64_t* x_stride, const float* weight,
                                    const float* bias, const float* state_in, const float* dout,
                                    float* dx, float* dweight, float* dbias, mmb_stream_t stream) {
+    MMB_NVTX("mmb_conv1d_silu_bwd");
     ConvParams p;
     int st = conv_fill(batch, seqlen, dim, width, x, x_stride, weight, bias, p);
     if (st != MMB_OK) return st;
@@ -307,6 +309,7 @@ extern "C" int mmb_conv1d_step(int64_t batch, int64_t dim, int32_t width, const 
                                int64_t x_row_stride, const float* state_in, float* state_out,
                                const float* weight, const float* bias, float* out,
                                mmb_stream_t stream) {
+    MMB_NVTX("mmb_conv1d_step");
     if (!x || !state_in || !state_out || !weight || !out) return MMB_ERR_NULL;
     if (batch <= 0 || dim <= 0) return MMB_ERR_SHAPE;
     if (width < 2 || width > CV_MAXW) return MMB_ERR_UNSUPPORTED;
@@ -321,6 +324,7 @@ extern "C" int mmb_mmscan_step(const mmb_step_desc* desc, const float* x, const 
                                const float* z, const float* delta_bias, const float* h_in,
                                const float* v_in, float* h, float* v, float* out,
                                mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_step");
     if (!desc || !x || !delta || !A || !B || !C || !h || !v || !out) return MMB_ERR_NULL;
     if (desc->batch <= 0 || desc->dim <= 0 || desc->dstate <= 0 || desc->dstate > 256)
         return MMB_ERR_SHAPE;

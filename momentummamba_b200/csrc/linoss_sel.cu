@@ -452,6 +452,7 @@ extern "C" int mmb_linoss_sel_fwd(int32_t disc, int64_t batch, int64_t L, int64_
                                   const float* B_im, const int64_t* B_stride, const float* C_re,
                                   const float* C_im, const int64_t* C_stride, float* y,
                                   float* work, mmb_stream_t stream) {
+    MMB_NVTX("mmb_linoss_sel_fwd");
     LSParams q;
     int st = ls_fill(disc, batch, L, P, A_diag, s, B_re, B_im, B_stride, C_re, C_im, C_stride,
                      work, q);
@@ -476,6 +477,7 @@ extern "C" int mmb_linoss_sel_bwd(int32_t disc, int64_t batch, int64_t L, int64_
                                   const float* C_im, const int64_t* C_stride, const float* dy,
                                   float* dB_re, float* dB_im, float* dC_re, float* dC_im,
                                   float* dA_diag, float* ds, float* work, mmb_stream_t stream) {
+    MMB_NVTX("mmb_linoss_sel_bwd");
     LSParams q;
     int st = ls_fill(disc, batch, L, P, A_diag, s, B_re, B_im, B_stride, C_re, C_im, C_stride,
                      work, q);

@@ -3,6 +3,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <nvtx3/nvToolsExt.h>
 #include <stdint.h>
 
 #include "../../include/momentum_scan_b200.h"
@@ -168,12 +169,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Wait for phase `parity` of the barrier, giving up after a bounded number of
-// polls (each poll itself suspends for a hardware-chosen while): false then.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
-    for (int i = 0; i < (1 << 22); ++i)
+// Wait for phase `parity` of the barrier, giving up after `polls` polls (each
+// poll itself suspends for a hardware-chosen while): false then.
+__device__ __forceinline__ bool mbar_wait_polls(uint64_t* bar, uint32_t parity, int polls) {
+    for (int i = 0; i < polls; ++i)
         if (mbar_try_wait(bar, parity)) return true;
     return false;
+}
+
+// The tile pipelines' wait: at most 2^22 polls.
+constexpr int MMB_WAIT_POLLS = 1 << 22;
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+    return mbar_wait_polls(bar, parity, MMB_WAIT_POLLS);
 }
 
 // 3-D tiled TMA load of the box at (c0, c1, c2) into shared memory, completing
@@ -410,6 +417,17 @@ int* mmb_device_error_flag();
 bool mmb_encode_tile_map(CUtensorMap* map, const void* base, int elem_bytes, int64_t dim0,
                          int64_t dim1, int64_t dim2, int64_t stride1, int64_t stride2,
                          int box0, int box1, int swizzle_bytes);
+
+// NVTX range around one C-ABI call (named after the entry point), so that a
+// profiler's timeline shows which library call launched which kernels.  NVTX3
+// is header-only; without a tool attached a range costs a few nanoseconds.
+struct MMBNvtxRange {
+    explicit MMBNvtxRange(const char* name) { nvtxRangePushA(name); }
+    ~MMBNvtxRange() { nvtxRangePop(); }
+    MMBNvtxRange(const MMBNvtxRange&) = delete;
+    MMBNvtxRange& operator=(const MMBNvtxRange&) = delete;
+};
+#define MMB_NVTX(name) MMBNvtxRange mmb_nvtx_range_(name)
 
 // Host-side launch-status helper shared by the C-ABI wrappers.
 static inline int mmb_launch_status() {

@@ -237,6 +237,7 @@ extern "C" int mmb_mmscan_fwd(const mmb_mmscan_desc* desc, const float* x, const
                               const float* A, const float* B, const float* C, const float* D,
                               const float* z, const float* delta_bias, float* out, float* ckpt,
                               mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_fwd");
     if (desc && desc->dtype != MMB_F32) return MMB_ERR_UNSUPPORTED;
     mmb_mmscan_tensors t{};
     t.x = x; t.delta = delta; t.z = z; t.B = B; t.C = C; t.A = A; t.D = D; t.delta_bias = delta_bias;
@@ -251,6 +252,7 @@ extern "C" int mmb_mmscan_bwd(const mmb_mmscan_desc* desc, const float* x, const
                               const float* dout, float* dx, float* ddelta, float* dA, float* dB,
                               float* dC, float* dD, float* dz, float* ddelta_bias,
                               mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_bwd");
     if (desc && desc->dtype != MMB_F32) return MMB_ERR_UNSUPPORTED;
     mmb_mmscan_tensors t{};
     t.x = x; t.delta = delta; t.z = z; t.B = B; t.C = C; t.A = A; t.D = D; t.delta_bias = delta_bias;
@@ -263,16 +265,19 @@ extern "C" int mmb_mmscan_bwd(const mmb_mmscan_desc* desc, const float* x, const
 
 extern "C" int mmb_mmscan_forward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t,
                                   mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_forward");
     return forward(desc, t, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int mmb_mmscan_backward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t,
                                    mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_backward");
     return backward(desc, t, reinterpret_cast<cudaStream_t>(stream));
 }
 
 extern "C" int mmb_mmscan_fwd_summary(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t,
                                       float* summary, mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_fwd_summary");
     if (!t) return MMB_ERR_NULL;
     MMParams p;
     // the summary reads x, delta, B, A, delta_bias only
@@ -287,6 +292,7 @@ extern "C" int mmb_mmscan_fwd_summary(const mmb_mmscan_desc* desc, const mmb_mms
 
 extern "C" int mmb_mmscan_bwd_summary(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t,
                                       float* gsummary, mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_bwd_summary");
     if (!t) return MMB_ERR_NULL;
     MMParams p;
     // reads delta, z, dout, C, A, delta_bias
@@ -304,6 +310,7 @@ extern "C" int mmb_mmscan_carry_fwd(int64_t nseg, int64_t seg, const int64_t* se
                                     int64_t batch, int64_t dim, int64_t dstate, float beta,
                                     const float* summaries, float* state_in,
                                     mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_carry_fwd");
     CarryArgs a;
     const int st = carry_args(nseg, seg, seg_len, batch, dim, dstate, beta, a);
     if (st != MMB_OK) return st;
@@ -317,6 +324,7 @@ extern "C" int mmb_mmscan_carry_bwd(int64_t nseg, int64_t seg, const int64_t* se
                                     int64_t batch, int64_t dim, int64_t dstate, float beta,
                                     const float* summaries, const float* gsummaries,
                                     float* gstate_in, mmb_stream_t stream) {
+    MMB_NVTX("mmb_mmscan_carry_bwd");
     CarryArgs a;
     const int st = carry_args(nseg, seg, seg_len, batch, dim, dstate, beta, a);
     if (st != MMB_OK) return st;

@@ -238,6 +238,7 @@ using namespace mmb;
 
 extern "C" int mmb_rows_fwd(int64_t rows, int64_t L, const float* a, float beta, const float* u,
                             float* h, float* v_out, mmb_stream_t stream) {
+    MMB_NVTX("mmb_rows_fwd");
     if (!a || !u || !h) return MMB_ERR_NULL;
     if (rows <= 0 || L <= 0) return MMB_ERR_SHAPE;
     const int vec = (L % 4 == 0) && al16(a) && al16(u) && al16(h) && al16(v_out);
@@ -254,6 +255,7 @@ extern "C" int mmb_rows_fwd(int64_t rows, int64_t L, const float* a, float beta,
 
 extern "C" int mmb_rows_bwd(int64_t rows, int64_t L, const float* g, const float* a, float beta,
                             const float* h, float* da, float* du, mmb_stream_t stream) {
+    MMB_NVTX("mmb_rows_bwd");
     if (!g || !a || !h) return MMB_ERR_NULL;
     if (rows <= 0 || L <= 0) return MMB_ERR_SHAPE;
     if (!da && !du) return MMB_OK;
@@ -271,6 +273,7 @@ extern "C" int mmb_rows_bwd(int64_t rows, int64_t L, const float* g, const float
 
 extern "C" int mmb_pscan_fwd(int64_t batch, int64_t L, int64_t M, const float* A, const float* X,
                              float* H, mmb_stream_t stream) {
+    MMB_NVTX("mmb_pscan_fwd");
     if (!A || !X || !H) return MMB_ERR_NULL;
     if (batch <= 0 || L <= 0 || M <= 0) return MMB_ERR_SHAPE;
     const int64_t nblk = (batch * M + PS_NT - 1) / PS_NT;
@@ -282,6 +285,7 @@ extern "C" int mmb_pscan_fwd(int64_t batch, int64_t L, int64_t M, const float* A
 
 extern "C" int mmb_pscan_bwd(int64_t batch, int64_t L, int64_t M, const float* A, const float* H,
                              const float* G, float* dA, float* dX, mmb_stream_t stream) {
+    MMB_NVTX("mmb_pscan_bwd");
     if (!A || !H || !G) return MMB_ERR_NULL;
     if (batch <= 0 || L <= 0 || M <= 0) return MMB_ERR_SHAPE;
     if (!dA && !dX) return MMB_OK;

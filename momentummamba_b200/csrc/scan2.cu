@@ -857,6 +857,7 @@ extern "C" size_t mmb_scan2_work_floats(int64_t batch, int64_t L, int64_t P, int
 extern "C" int mmb_scan2_fwd(int64_t batch, int64_t L, int64_t P, int32_t complex_f,
                              const float* M, const float* F, float* Mscan, float* X, float* work,
                              mmb_stream_t stream) {
+    MMB_NVTX("mmb_scan2_fwd");
     if (!M || !F || !X) return MMB_ERR_NULL;
     if (!work) return MMB_ERR_WORKSPACE;
     if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
@@ -873,6 +874,7 @@ extern "C" int mmb_scan2_bwd(int64_t batch, int64_t L, int64_t P, int32_t comple
                              const float* M, const float* X, const float* gX, const float* Mscan,
                              const float* gMscan, float* dM, float* dF, float* work,
                              mmb_stream_t stream) {
+    MMB_NVTX("mmb_scan2_bwd");
     if (!M || !X || !dM || !dF) return MMB_ERR_NULL;
     if (gMscan && !Mscan) return MMB_ERR_NULL;
     if (!work) return MMB_ERR_WORKSPACE;
@@ -897,6 +899,7 @@ extern "C" size_t mmb_linoss_work_floats(int64_t batch, int64_t L, int64_t P) {
 extern "C" int mmb_linoss_fwd(int32_t disc, int64_t batch, int64_t L, int64_t P,
                               const float* A_diag, const float* step, const float* Bu, float* x2,
                               float* work, mmb_stream_t stream) {
+    MMB_NVTX("mmb_linoss_fwd");
     if (!A_diag || !step || !Bu || !x2) return MMB_ERR_NULL;
     if (!work) return MMB_ERR_WORKSPACE;
     if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
@@ -916,6 +919,7 @@ extern "C" int mmb_linoss_bwd(int32_t disc, int64_t batch, int64_t L, int64_t P,
                               const float* A_diag, const float* step, const float* Bu,
                               const float* dx2, float* dBu, float* dA_diag, float* dstep,
                               float* work, mmb_stream_t stream) {
+    MMB_NVTX("mmb_linoss_bwd");
     if (!A_diag || !step || !Bu || !dx2 || !dBu) return MMB_ERR_NULL;
     if (!work) return MMB_ERR_WORKSPACE;
     if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
@@ -958,6 +962,7 @@ float* g_noalloc_scratch[MMB_MAX_DEVICES] = {};
 extern "C" int mmb_scan2_fwd_noalloc(int64_t batch, int64_t L, int64_t P, int32_t complex_f,
                                      const float* M, const float* F, float* Mscan, float* X,
                                      mmb_stream_t stream) {
+    MMB_NVTX("mmb_scan2_fwd_noalloc");
     if (!M || !F || !X) return MMB_ERR_NULL;
     if (batch <= 0 || L <= 0 || P <= 0) return MMB_ERR_SHAPE;
     // one summary and one carry record of S2_REC floats per (b, chunk, p)

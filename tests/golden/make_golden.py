@@ -3,7 +3,7 @@
 Run once, in a container that has the reference checkout (it is not needed
 afterwards; the fixtures are committed):
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/reference
 
 Every fixture stores the seeded inputs, the upstream gradient it used, and the
 reference's outputs and autograd gradients, all as float32 (complex64 for
@@ -280,7 +280,9 @@ def gen_state_dict(ref):
 
 
 def main():
-    refdir = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) != 2:
+        sys.exit("usage: python tests/golden/make_golden.py <reference source directory>")
+    refdir = sys.argv[1]
     sys.path.insert(0, refdir)
     import importlib
     ref = {m: importlib.import_module(m)

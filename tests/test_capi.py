@@ -100,3 +100,10 @@ def test_module_tree_matches_reference_state_dict(golden_dir):
     m = MambaMomentum(MambaMomentumConfig(d_model=128, n_layers=2, dt_rank=8))
     got = {k: list(v.shape) for k, v in m.state_dict().items()}
     assert got == want
+
+
+def test_selftest_wait_rejects_out_of_range_poll_counts():
+    # checked before any device work: no GPU needed
+    lib = _lib.load()
+    assert lib.mmb_selftest_device_wait(0, None) == 2       # MMB_ERR_SHAPE
+    assert lib.mmb_selftest_device_wait(4097, None) == 2

@@ -153,3 +153,71 @@ def test_sequence_sharded_protocol_matches_the_whole_sequence(seg_lens):
         else:
             got = np.concatenate([r[2][k] for r in res], 1)
             assert rel(got, want) < 1e-10, k
+
+
+class _InjectedFault(RuntimeError):
+    pass
+
+
+def _faulty_worker(rank, world, port, seg_lens, fail_rank, q):
+    """One rank of the protocol whose rank `fail_rank` raises between the forward
+    all-gather and the carry fold, then leaves without another collective."""
+    import datetime
+    import time
+    import torch.distributed as dist
+
+    class FaultyOps(OracleOps):
+        @staticmethod
+        def carry_fwd(summ, seg, lens, beta):
+            if seg == fail_rank:
+                raise _InjectedFault(f"rank {seg}: injected failure before the fold")
+            return OracleOps.carry_fwd(summ, seg, lens, beta)
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=10))
+    t0 = time.monotonic()
+    outcome = "finished"
+    try:
+        from momentummamba_b200.seqshard import seq_sharded_selective_scan
+        L = sum(seg_lens)
+        g = _inputs(L)
+        a, b = sum(seg_lens[:rank]), sum(seg_lens[: rank + 1])
+        seg = lambda k: torch.from_numpy(np.ascontiguousarray(g[k][:, a:b])).requires_grad_()
+        x, delta, B, C, z = (seg(k) for k in ("x", "delta", "B", "C", "z"))
+        A, D, bias = (torch.from_numpy(g[k]).requires_grad_() for k in ("A", "D", "bias"))
+        y = seq_sharded_selective_scan(x, delta, A, B, C, D, z, bias, True, BETA, ALPHA,
+                                       seg_lens=seg_lens, ops=FaultyOps)
+        y.backward(torch.from_numpy(np.ascontiguousarray(g["dout"][:, a:b])))
+    except _InjectedFault:
+        outcome = "injected"
+    except Exception as e:  # the survivors: the next collective must fail, not hang
+        outcome = f"error: {type(e).__name__}"
+    q.put((rank, outcome, time.monotonic() - t0))
+    q.close()
+    q.join_thread()
+    os._exit(0)  # leave without destroy_process_group: a rank that died
+
+
+@pytest.mark.parametrize("seg_lens,fail_rank", [((48, 53), 1), ((40, 16, 37), 1)])
+def test_a_failing_rank_ends_the_others_collectives_with_an_error(seg_lens, fail_rank):
+    """A rank that raises between the forward all-gather and the fold and then
+    leaves: every other rank gets an error from its next collective within the
+    process-group timeout (10 s) instead of waiting for good."""
+    world, port = len(seg_lens), _free_port()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_faulty_worker,
+                         args=(r, world, port, list(seg_lens), fail_rank, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=120) for _ in range(world)), key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=60)
+    for rank, outcome, secs in res:
+        if rank == fail_rank:
+            assert outcome == "injected"
+        else:
+            assert outcome.startswith("error"), (rank, outcome)
+            assert secs < 60.0, (rank, secs)

@@ -115,8 +115,11 @@ def test_apply_linoss_vectorized_golden(golden_dir, disc):
         close(gr, g["d" + k], "d" + k)
 
 
+# (1, 1125, 3): 71 chunks of 16 steps (more than two warp rounds of the chunk
+# carry scan) and a ragged last chunk of 5 steps
 @pytest.mark.parametrize("Bsz,L,P,cplx", [(3, 1000, 40, True), (2, 37, 5, False), (1, 1, 3, True),
-                                          (4, 4096, 64, True)])
+                                          (4, 4096, 64, True), (1, 16 * 70 + 5, 3, True),
+                                          (1, 16 * 70 + 5, 3, False)])
 def test_scan2_random_vs_oracle(Bsz, L, P, cplx):
     from momentummamba_b200.scan2 import scan2
     rng = np.random.default_rng(L * 7 + P)

@@ -14,18 +14,32 @@ This file is collected last on purpose, so that a run stopping at the first
 failure has already run every other test.
 """
 import ctypes
+import os
+import re
 
 import numpy as np
 import pytest
 import torch
 
+import oracle
 from momentummamba_b200 import _lib
 
 pytestmark = pytest.mark.gpu
 
 TOL = 1e-4
 DEV = "cuda:0"
-SCRATCH_FLOATS = 1 << 20  # MMB_SCAN2_NOALLOC_SCRATCH_FLOATS
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _scratch_floats():
+    """MMB_SCAN2_NOALLOC_SCRATCH_FLOATS as the header defines it."""
+    src = open(os.path.join(ROOT, "include", "momentum_scan_b200.h")).read()
+    m = re.search(r"#define\s+MMB_SCAN2_NOALLOC_SCRATCH_FLOATS\s+\(1 << (\d+)\)", src)
+    assert m, "MMB_SCAN2_NOALLOC_SCRATCH_FLOATS not found in the header"
+    return 1 << int(m.group(1))
+
+
+SCRATCH_FLOATS = _scratch_floats()
 
 
 def _noalloc(lib):
@@ -56,7 +70,10 @@ def test_noalloc_matches_allocating_entry_point(order):
     fn = _noalloc(lib)
     P_ = _lib.ptr
     cases = [(8, 2048, 256, True, True),    # chunk count capped by the fixed scratch
-             (2, 333, 17, False, False)]    # ragged, real, no running product
+             (2, 333, 17, False, False),    # ragged, real, no running product
+             # batch * P = 65536 chains: the scratch holds one chunk, so every chain
+             # runs its whole (ragged) length as one chunk
+             (1, 37, SCRATCH_FLOATS // 16, False, False)]
     if order == "small_first":
         cases = cases[::-1]
     for seed, (Bsz, L, P, cplx, want_ms) in enumerate(cases):
@@ -78,6 +95,13 @@ def test_noalloc_matches_allocating_entry_point(order):
         assert _rel(X, Xr) <= TOL
         if want_ms:
             assert _rel(Ms, Msr) <= TOL
+        if Bsz * L * P <= 1 << 16:  # small enough for the fp64 CPU oracle as well
+            Fo = F.cpu().numpy()
+            Fo = Fo[..., 0] + 1j * Fo[..., 1] if cplx else Fo[..., 0]
+            _, Xo = oracle.scan2_fwd(M.cpu().numpy(), Fo)
+            Xg = X.cpu().numpy()
+            Xg = Xg[..., 0] + 1j * Xg[..., 1] if cplx else Xg[..., 0]
+            assert oracle.rel_err(Xg, Xo) <= TOL
 
 
 def test_noalloc_rejects_problems_beyond_the_scratch():
