@@ -11,6 +11,10 @@ are independent, so the data path has no collective.
 
 Extra keys of the same line (each with its own roofline):
   * ``stack_cfg1``: the 4-layer stack of d_model 128 (B=32 L=1024 D=256 N=16);
+  * ``time_chunks``: 4 layers of B=2 L=8192 D=256 N=16, too few channels to
+                    fill the GPU, so each call splits the sequence into time
+                    chunks scanned by separate CTAs (with the unsplit calls'
+                    times beside);
   * ``long_seq``:   B=8 L=65536 D=2048 N=16 in bf16, split along time over the
                     ranks (segment summaries all-gathered over NCCL);
   * ``linoss``:     the LinOSS layer scan, IM and IMEX, B=16 L=4096 P=256;
@@ -18,7 +22,7 @@ Extra keys of the same line (each with its own roofline):
 On N > 1 GPUs only ``long_seq`` runs beside the default line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload classifier|stack|long|linoss|rows] [--no-extras]
+                    [--workload classifier|stack|chunks|long|linoss|rows] [--no-extras]
 
 Rank 0 prints ONE JSON line.  ``--impl reference`` times the CPU restatement
 of the reference algorithm (oracle/, fp32 variant, all host threads) on a
@@ -48,6 +52,9 @@ BETA, ALPHA = 0.6, 1.0
 CLASSIFIER = dict(batch=256, seqlen=300, dim=512, dstate=16, layers=6)
 # MambaMomentum stack of d_model 128, expand 2: 4 layers
 STACK1 = dict(batch=32, seqlen=1024, dim=256, dstate=16, layers=4)
+# short batch of long sequences (d_model 128, expand 2): 512 channels give the
+# GPU 64 warps, so each call splits along time (chunks scanned by separate CTAs)
+CHUNKED = dict(batch=2, seqlen=8192, dim=256, dstate=16, layers=4, compare_unsplit=True)
 
 
 def fwd_bytes(Bsz, L, D, N):
@@ -273,8 +280,9 @@ class Layer:
         self.dbias = torch.empty_like(self.D)
 
 
-def make_desc(_lib, Bsz, L, D, N):
+def make_desc(_lib, Bsz, L, D, N, time_chunk=0):
     d = _lib.MMScanDesc()
+    d.time_chunk = time_chunk
     d.batch, d.seqlen, d.dim, d.dstate = Bsz, L, D, N
     d.x_stride[:] = (L * D, D)
     d.delta_stride[:] = (L * D, D)
@@ -309,13 +317,13 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
     desc = make_desc(_lib, Bsz, L, D, N)
     P = _lib.ptr
 
-    def fwd(ly):
-        st = lib.mmb_mmscan_fwd(desc, P(ly.x), P(ly.delta), P(ly.A), P(ly.B), P(ly.C), P(ly.D),
+    def fwd(ly, dsc=desc):
+        st = lib.mmb_mmscan_fwd(dsc, P(ly.x), P(ly.delta), P(ly.A), P(ly.B), P(ly.C), P(ly.D),
                                 P(ly.z), P(ly.bias), P(ly.out), P(ly.ckpt), _lib.stream_of(ly.x))
         _lib.check(st, "fwd")
 
-    def bwd(ly):
-        st = lib.mmb_mmscan_bwd(desc, P(ly.x), P(ly.delta), P(ly.A), P(ly.B), P(ly.C), P(ly.D),
+    def bwd(ly, dsc=desc):
+        st = lib.mmb_mmscan_bwd(dsc, P(ly.x), P(ly.delta), P(ly.A), P(ly.B), P(ly.C), P(ly.D),
                                 P(ly.z), P(ly.bias), P(ly.ckpt), P(ly.dout), P(ly.dx),
                                 P(ly.ddelta), P(ly.dA), P(ly.dB), P(ly.dC), P(ly.dD), P(ly.dz),
                                 P(ly.dbias), _lib.stream_of(ly.x))
@@ -354,6 +362,14 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
     t = launch_times([("fwd", lambda: fwd(layers[0])), ("bwd", lambda: bwd(layers[1]))], reps=10)
     t_fwd = ctx_max(t["fwd"], ctx)
     t_bwd = ctx_max(t["bwd"], ctx)
+    unsplit = None
+    if cfg.get("compare_unsplit"):
+        # the same calls with the split along time turned off
+        d1 = make_desc(_lib, Bsz, L, D, N, time_chunk=-1)
+        u = launch_times([("fwd", lambda: fwd(layers[0], d1)), ("bwd", lambda: bwd(layers[1], d1))],
+                         reps=5)
+        unsplit = {"fwd_ms": ctx_max(u["fwd"], ctx), "bwd_ms": ctx_max(u["bwd"], ctx)}
+    nch = -(-L // chunk_len(lib, _lib, desc))
     del graph
 
     e2e = None
@@ -375,6 +391,9 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
     workload = (f"{NL}-layer momentum-Mamba scan fwd+bwd (expand 2, d_state {N}): "
                 f"B={Btot} L={L} D={D} N={N} per layer, softplus(delta+bias) and SiLU(z) "
                 f"gate fused, fp32")
+    if nch > 1:
+        workload += (f"; each call split along time into {nch} chunks (summary, carry and "
+                     f"full passes)")
     par = (f"batch split over {ctx.world} rank(s): {Bsz} sequences each, no data-path "
            f"collective" if strong else f"batch-sharded replicas x{ctx.world}: {Bsz} "
            f"sequences per rank, no data-path collective")
@@ -389,7 +408,10 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
                    "l2": f"inputs larger than L2: {NL} layers x "
                          f"{fwd_bytes(Bsz, L, D, N) / 1e6:.0f} MB of scan inputs per step"},
         "roofline": {
-            "kernel": f"mmscan_bwd_kernel<{N}>", "bound": "hbm", "achieved": achieved,
+            "kernel": (f"mmscan_bwd_kernel<{N}>" if nch == 1 else
+                       f"backward call: clearing + summary + carry + mmscan_bwd_kernel<{N}> "
+                       f"over {nch} time chunks"),
+            "bound": "hbm", "achieved": achieved,
             "peak": peak, "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s",
             "frac": achieved / peak,
             "traffic": traffic.get("dram_bytes_per_launch") if traffic else None,
@@ -404,12 +426,25 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
                                         "GB/s": achieved, "frac": achieved / peak},
         },
         "hbm_gbs_step": NL * (fb + bb) * steps / (ms / 1e3) / 1e9,
+        "time_chunks": nch,
+        "unsplit": unsplit,
         "e2e": e2e,
-        # per layer: forward, clearing of the backward's sums, backward
-        "gpu_launches": 3 * NL * steps,
+        # per layer: forward, clearing of the backward's sums, backward; split
+        # calls add a summary and a carry launch to each side
+        "gpu_launches": (3 + (4 if nch > 1 else 0)) * NL * steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+
+
+def chunk_len(lib, _lib, desc):
+    """Steps per time chunk the library uses for desc (the sequence length when
+    it does not split), from the workspace it asks for."""
+    import ctypes
+    Bsz, L, D, N = desc.batch, desc.seqlen, desc.dim, desc.dstate
+    extra = lib.mmb_mmscan_workspace_floats(ctypes.byref(desc)) - Bsz * (-(-L // 8)) * D * N * 2
+    nch = extra // (Bsz * D * N * 6) if extra else 1
+    return -(-L // nch)
 
 
 def run_e2e(torch, fn, ctx, layers, cfg, steps=4):
@@ -952,7 +987,8 @@ def summary(line):
     if line is None:
         return None
     keep = ("value", "unit", "n_gpus", "steps", "ms_per_step", "scaling", "dtype", "config",
-            "roofline", "kernels", "phases_ms", "gpu_launches", "clocks", "cpu_baseline")
+            "roofline", "kernels", "time_chunks", "unsplit", "phases_ms", "gpu_launches",
+            "clocks", "cpu_baseline")
     return {k: line[k] for k in keep if k in line}
 
 
@@ -967,12 +1003,14 @@ def main():
     ap.add_argument("--no-extras", action="store_true",
                     help="default workload only (no extra keys)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--workload", choices=["classifier", "stack", "long", "linoss", "rows"],
+    ap.add_argument("--workload", choices=["classifier", "stack", "chunks", "long", "linoss",
+                                           "rows"],
                     default="classifier",
                     help="classifier: the 6-layer momentum-Mamba classifier scan, B=256 T=300 "
                          "D=512 split over the ranks (the benchmark line, with the other "
                          "workloads as extra keys); stack: the 4-layer d_model-128 stack, "
-                         "B=32 L=1024 D=256 per rank; long: B=8 L=65536 D=2048 bf16, "
+                         "B=32 L=1024 D=256 per rank; chunks: 4 layers of B=2 L=8192 D=256 "
+                         "split along time inside the GPU; long: B=8 L=65536 D=2048 bf16, "
                          "sequence-sharded; linoss: the LinOSS layer scan, IM and IMEX, "
                          "B=16 L=4096 P=256; rows: the row-form and PScan-layout scans")
     ap.add_argument("--kernels-only", action="store_true",
@@ -1004,6 +1042,9 @@ def main():
                                                          name="stack_cfg1"))
             extras["long_seq"] = summary(run_long(ctx, max(3, K // 40)))
             if ctx.world == 1:
+                extras["time_chunks"] = summary(run_stack(ctx, CHUNKED, False, K,
+                                                          with_e2e=False, with_cpu=False,
+                                                          name="time_chunks"))
                 extras["linoss"] = summary(run_linoss(ctx, 2 * K))
                 extras["rows"] = summary(run_rows(ctx, max(3, K // 4)))
             if line is not None:
@@ -1012,6 +1053,9 @@ def main():
                     (v or {}).get("gpu_launches", 0) for v in extras.values())
     elif args.workload == "stack":
         line = run_stack(ctx, STACK1, False, K, with_e2e=True, with_cpu=True, name="stack_cfg1")
+    elif args.workload == "chunks":
+        line = run_stack(ctx, CHUNKED, False, K, with_e2e=False, with_cpu=False,
+                         name="time_chunks")
     elif args.workload == "long":
         line = run_long(ctx, K)
     elif args.workload == "linoss":

@@ -101,14 +101,39 @@ typedef struct mmb_mmscan_desc {
     float beta, alpha;
     int32_t delta_softplus;
     int32_t dtype;           /* enum mmb_dtype (0 = fp32)     */
+    int32_t time_chunk;      /* steps per time chunk: 0 = the library's choice,
+                                < 0 = never split, > 0 = this many (rounded up
+                                to a multiple of 32)                          */
+    int32_t reserved;        /* 0 */
 } mmb_mmscan_desc;
 
-/* Floats of checkpoint workspace the forward writes for the backward
- * (the (h, v) state every 8 steps): batch * ceil(seqlen/8) * dim * dstate * 2. */
+/* Time chunks.  When batch x dim gives the GPU few warps (short batches of
+ * long sequences), mmb_mmscan_fwd / mmb_mmscan_bwd cut the sequence into
+ * chunks that separate CTAs scan at once: a summary pass gives each chunk its
+ * affine map (forward: end state from zero and the products P, Q'; backward:
+ * the adjoint pair from zero and the same P, Q'), a small kernel folds the maps
+ * into every chunk's incoming carry, and the full pass runs each chunk from it.
+ * The library splits on its own when batch * ceil(dim * dstate / 128) < 592
+ * (four one-warp backward CTAs per SM), aiming at sixteen per SM in chunks of
+ * at least 256 steps; desc.time_chunk overrides that.  Calls that pass state_in, state_out,
+ * gstate_in or gstate_out, and forwards without checkpoints, never split.
+ * The forward and the backward split independently (the backward does not read
+ * the forward's carries), so each may take its own path. */
+
+/* Floats of workspace for a call: the checkpoints the forward writes for the
+ * backward ((h, v) every 8 steps, batch * ceil(seqlen/8) * dim * dstate * 2)
+ * followed, when the call splits along time, by scratch for the chunk carries
+ * (chunks * batch * dim * dstate * 6) that the forward and the backward both
+ * write. */
+size_t mmb_mmscan_workspace_floats(const mmb_mmscan_desc* desc);
+
+/* The same for a descriptor with these sizes and time_chunk = 0 (the
+ * library's choice). */
 size_t mmb_mmscan_ckpt_floats(int64_t batch, int64_t seqlen, int64_t dim, int64_t dstate);
 
-/* Forward.  D, z, delta_bias nullable.  ckpt nullable (inference: no
- * checkpoints); the backward needs the checkpoints of the same call.
+/* Forward.  D, z, delta_bias nullable.  ckpt (mmb_mmscan_workspace_floats
+ * floats) nullable (inference: no checkpoints, no time split); the backward
+ * needs the checkpoints of the same call.
  * fp32 activations only (desc->dtype == MMB_F32); mmb_mmscan_forward takes
  * either type and the segment carries. */
 int mmb_mmscan_fwd(const mmb_mmscan_desc* desc, const float* x, const float* delta,
@@ -116,12 +141,14 @@ int mmb_mmscan_fwd(const mmb_mmscan_desc* desc, const float* x, const float* del
                    const float* z, const float* delta_bias, float* out, float* ckpt,
                    mmb_stream_t stream);
 
-/* Backward.  Inputs as in the forward plus ckpt (required) and dout.
+/* Backward.  Inputs as in the forward plus ckpt (required: the workspace of
+ * the forward, whose scratch past the checkpoints the backward also writes)
+ * and dout.
  * Outputs dx, ddelta, dA, dB, dC are required; dD (when D given), dz (when z
  * given) and ddelta_bias (when delta_bias given) are nullable. */
 int mmb_mmscan_bwd(const mmb_mmscan_desc* desc, const float* x, const float* delta,
                    const float* A, const float* B, const float* C, const float* D,
-                   const float* z, const float* delta_bias, const float* ckpt,
+                   const float* z, const float* delta_bias, float* ckpt,
                    const float* dout, float* dx, float* ddelta, float* dA, float* dB,
                    float* dC, float* dD, float* dz, float* ddelta_bias,
                    mmb_stream_t stream);

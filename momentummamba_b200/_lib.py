@@ -31,6 +31,7 @@ class MMScanDesc(ctypes.Structure):
         ("x_stride", _c_i64 * 2), ("delta_stride", _c_i64 * 2), ("z_stride", _c_i64 * 2),
         ("B_stride", _c_i64 * 2), ("C_stride", _c_i64 * 2),
         ("beta", _c_f), ("alpha", _c_f), ("delta_softplus", _c_i32), ("dtype", _c_i32),
+        ("time_chunk", _c_i32), ("reserved", _c_i32),
     ]
 
 
@@ -68,6 +69,7 @@ _SIGNATURES = {
     "mmb_device_status": (ctypes.c_int, [_c_p]),
     "mmb_selftest_device_wait": (ctypes.c_int, [_c_i32, _c_p]),
     "mmb_mmscan_ckpt_floats": (_c_size, [_c_i64, _c_i64, _c_i64, _c_i64]),
+    "mmb_mmscan_workspace_floats": (_c_size, [_DESC_P]),
     "mmb_mmscan_fwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 10 + [_c_p]),
     "mmb_mmscan_bwd": (ctypes.c_int, [ctypes.POINTER(MMScanDesc)] + [_c_p] * 18 + [_c_p]),
     "mmb_mmscan_forward": (ctypes.c_int, [_DESC_P, _TENS_P, _c_p]),

@@ -3,7 +3,7 @@
 
 #include "mmb_common.cuh"
 
-#define MMB_ABI_VERSION 2
+#define MMB_ABI_VERSION 3
 
 extern "C" const char* mmb_status_string(int status) {
     switch (status) {

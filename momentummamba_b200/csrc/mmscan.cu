@@ -12,10 +12,132 @@ namespace mmb {
 #ifndef MMB_NP2_THRESHOLD_WARPS_PER_SM
 #define MMB_NP2_THRESHOLD_WARPS_PER_SM 2
 #endif
-static int states_per_thread(const MMParams& p, int64_t N, int dtype) {
-    if (N == 64 || dtype == MMB_BF16) return 4;
-    const int64_t threads4 = p.Bsz * p.D * (N / 4);
+static int64_t time_chunks(const mmb_mmscan_desc* desc);
+
+static int states_per_thread(const mmb_mmscan_desc* desc) {
+    const int64_t N = desc->dstate;
+    if (N == 64 || desc->dtype == MMB_BF16) return 4;
+    const int64_t threads4 = desc->batch * desc->dim * (N / 4) * time_chunks(desc);
     return threads4 < (int64_t)148 * MMB_NP2_THRESHOLD_WARPS_PER_SM * 32 ? 2 : 4;
+}
+
+// ---------------------------------------------------------------------------
+// Time chunks.  When the (sequence, channel) pairs of a call give the GPU too
+// few warps, the sequence is cut into chunks of T_c steps that separate CTAs
+// scan at once: a summary pass gives every chunk its affine map, a carry kernel
+// folds the maps into each chunk's incoming state (forward) or adjoint pair
+// (backward), and the full pass runs every chunk from its carry.
+// ---------------------------------------------------------------------------
+// Warps (one-warp backward CTAs of 128 / N channels) below which the library
+// splits, and the warps it then aims for.  Measured per call (fwd / bwd, us,
+// N = 16, D = 256): B=32 L=1024 (1024 warps) runs 122 / 226 unsplit and
+// slower split (130-137 / 288-296); B=8 L=4096 (256 warps) 258 / 495 unsplit,
+// 147 / 298 in chunks of 256; B=1 L=65536 (32 warps) 3874 / 7692 unsplit,
+// 289 / 601 in chunks of 512.  More chunks than SMs can hold at once still
+// pay: the summaries cost a fraction of the full pass.
+constexpr int64_t MM_SPLIT_WARPS = 148 * 4;
+constexpr int64_t MM_TARGET_WARPS = 148 * 16;
+constexpr int64_t MM_MIN_AUTO_CHUNK = 256;  // shortest chunk the library picks
+
+// Steps per time chunk of a call (a multiple of MM_T; >= seqlen: no split).
+static int64_t time_chunk_len(const mmb_mmscan_desc* desc) {
+    const int64_t L = desc->seqlen;
+    int64_t tc;
+    if (desc->time_chunk < 0) return L;
+    if (desc->time_chunk > 0) {
+        tc = desc->time_chunk;
+    } else {
+        const int64_t warps = desc->batch * ((desc->dim * desc->dstate + 127) / 128);
+        if (warps >= MM_SPLIT_WARPS) return L;
+        const int64_t want = (MM_TARGET_WARPS + warps - 1) / warps;
+        tc = (L + want - 1) / want;
+        if (tc < MM_MIN_AUTO_CHUNK) tc = MM_MIN_AUTO_CHUNK;
+    }
+    tc = (tc + MM_T - 1) / MM_T * MM_T;
+    // grid z holds the chunks
+    while ((L + tc - 1) / tc > 65535) tc *= 2;
+    return tc >= L ? L : tc;
+}
+
+static int64_t time_chunks(const mmb_mmscan_desc* desc) {
+    const int64_t tc = time_chunk_len(desc);
+    return (desc->seqlen + tc - 1) / tc;
+}
+
+// Floats of the checkpoints: (h, v) every 8 steps.
+static int64_t ckpt_floats(int64_t Bsz, int64_t L, int64_t D, int64_t N) {
+    return Bsz * ((L + MM_CK - 1) / MM_CK) * D * N * 2;
+}
+
+// Floats after the checkpoints for the chunk carries: per chunk and (b, d) the
+// summary [4N] and the carry [2N] (the forward's, then the backward's).
+static int64_t chunk_floats(const mmb_mmscan_desc* desc) {
+    const int64_t nch = time_chunks(desc);
+    return nch > 1 ? nch * desc->batch * desc->dim * desc->dstate * 6 : 0;
+}
+
+static double pow_int(double base, int64_t e) {
+    double r = 1.0;
+    for (; e > 0; e >>= 1) {
+        if (e & 1) r *= base;
+        base *= base;
+    }
+    return r;
+}
+
+// Incoming (h, v) of every chunk: zeros for chunk 0, then the fold of the
+// earlier chunks' summaries [h^0 | v^0 | P | Q'].  One thread per (b, d, n).
+__global__ void chunk_carry_fwd_kernel(int64_t BD, int N, int nch, float beta, float betaTc,
+                                       const float* __restrict__ summ,
+                                       float* __restrict__ state_in) {
+    const int64_t total = BD * N;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t bd = e / N, n = e % N;
+        float h = 0.f, v = 0.f;
+        for (int c = 0; c < nch; ++c) {
+            float* o = state_in + ((int64_t)c * BD + bd) * 2 * N;
+            o[n] = h;
+            o[N + n] = v;
+            if (c + 1 == nch) break;
+            const float* sm = summ + ((int64_t)c * BD + bd) * 4 * N;
+            const float hn = fmaf(sm[2 * N + n], h, fmaf(beta * sm[3 * N + n], v, sm[n]));
+            v = fmaf(betaTc, v, sm[N + n]);
+            h = hn;
+        }
+    }
+}
+
+// Adjoint pair arriving at the end of every chunk: zeros for the last chunk,
+// then the fold of the later chunks' summaries [lam^0 | mu^0 | P | Q'].
+__global__ void chunk_carry_bwd_kernel(int64_t BD, int N, int nch, float betaTc,
+                                       const float* __restrict__ gsumm,
+                                       float* __restrict__ gstate_in) {
+    const int64_t total = BD * N;
+    for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < total;
+         e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t bd = e / N, n = e % N;
+        float lam = 0.f, mu = 0.f;
+        for (int c = nch - 1; c >= 0; --c) {
+            float* o = gstate_in + ((int64_t)c * BD + bd) * 2 * N;
+            o[n] = lam;
+            o[N + n] = mu;
+            if (c == 0) break;
+            const float* g = gsumm + ((int64_t)c * BD + bd) * 4 * N;
+            if (c == nch - 1) {  // nothing arrives after the last chunk
+                lam = g[n];
+                mu = g[N + n];
+            } else {
+                mu = fmaf(g[3 * N + n], lam, fmaf(betaTc, mu, g[N + n]));
+                lam = fmaf(g[2 * N + n], lam, g[n]);
+            }
+        }
+    }
+}
+
+static unsigned chunk_carry_blocks(int64_t BD, int64_t N) {
+    const int64_t blocks = (BD * N + 255) / 256;
+    return (unsigned)(blocks < 148 * 16 ? blocks : 148 * 16);
 }
 
 static bool aligned16(const void* ptr) { return ptr == nullptr || ((uintptr_t)ptr & 15) == 0; }
@@ -46,6 +168,9 @@ static int fill_params(const mmb_mmscan_desc* desc, const void* x, const void* d
     p.beta = desc->beta;
     p.alpha = desc->alpha;
     p.softplus = desc->delta_softplus != 0;
+    p.tchunk = p.L;  // one time chunk unless the call splits
+    p.zoff = 0;
+    p.nz = 1;
     // 16-byte staging: 4 fp32 or 8 bf16 elements per copy
     const int64_t q = desc->dtype == MMB_BF16 ? 8 : 4;
     bool vec = aligned16(x) && aligned16(delta) && aligned16(z) && aligned16(B) && aligned16(C) &&
@@ -59,7 +184,7 @@ static int fill_params(const mmb_mmscan_desc* desc, const void* x, const void* d
 }
 
 static int launch(const mmb_mmscan_desc* desc, const MMParams& p, int kind, cudaStream_t s) {
-    const int np = states_per_thread(p, desc->dstate, desc->dtype);
+    const int np = states_per_thread(desc);
     const bool fwd = kind == MM_FWD || kind == MM_FWD_SUMMARY;
     if (desc->dtype == MMB_BF16)
         return fwd ? mmscan_launch<ElemBF16, true>(p, desc->dstate, np, kind, s)
@@ -80,6 +205,30 @@ static int forward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t, cud
     p.ckpt = t->ckpt;
     p.state_in = t->state_in;
     p.state_out = t->state_out;
+    const int64_t nch = time_chunks(desc);
+    if (nch <= 1 || !t->ckpt || t->state_in || t->state_out) return launch(desc, p, MM_FWD, s);
+
+    // split along time: chunk summaries, their fold, the full pass
+    const int64_t tc = time_chunk_len(desc), BD = p.Bsz * p.D, N = desc->dstate;
+    float* summ = t->ckpt + ckpt_floats(p.Bsz, p.L, p.D, N);
+    float* sin = summ + nch * BD * 4 * N;
+    MMParams ps = p;
+    ps.z = nullptr;
+    ps.Cm = nullptr;
+    ps.ckpt = nullptr;
+    ps.summary = summ;
+    ps.tchunk = tc;
+    ps.nz = (int)(nch - 1);
+    st = launch(desc, ps, MM_FWD_SUMMARY, s);
+    if (st != MMB_OK) return st;
+    const float betaTc = (float)pow_int((double)desc->beta, tc);
+    chunk_carry_fwd_kernel<<<chunk_carry_blocks(BD, N), 256, 0, s>>>(BD, (int)N, (int)nch,
+                                                                      desc->beta, betaTc, summ, sin);
+    st = mmb_launch_status();
+    if (st != MMB_OK) return st;
+    p.state_in = sin;
+    p.tchunk = tc;
+    p.nz = (int)nch;
     return launch(desc, p, MM_FWD, s);
 }
 
@@ -143,6 +292,32 @@ static int backward(const mmb_mmscan_desc* desc, const mmb_mmscan_tensors* t, cu
     zero_sums_kernel<<<(unsigned)blocks, 256, 0, s>>>(zl);
     const int zst = mmb_launch_status();
     if (zst != MMB_OK) return zst;
+    const int64_t nch = time_chunks(desc);
+    if (nch <= 1 || t->gstate_in || t->gstate_out) return launch(desc, p, MM_BWD, s);
+
+    // split along time: summaries of chunks 1.. (adjoint pair from zero and
+    // the chunk's P, Q'), their fold from the end, the full pass
+    const int64_t tc = time_chunk_len(desc), BD = p.Bsz * p.D;
+    float* gsumm = t->ckpt + ckpt_floats(p.Bsz, p.L, p.D, N);
+    float* gin = gsumm + nch * BD * 4 * N;
+    MMParams ps = p;
+    ps.x = nullptr;
+    ps.Bm = nullptr;
+    ps.summary = gsumm;
+    ps.bsum_pq = 1;
+    ps.tchunk = tc;
+    ps.zoff = 1;
+    ps.nz = (int)(nch - 1);
+    st = launch(desc, ps, MM_BWD_SUMMARY, s);
+    if (st != MMB_OK) return st;
+    const float betaTc = (float)pow_int((double)desc->beta, tc);
+    chunk_carry_bwd_kernel<<<chunk_carry_blocks(BD, N), 256, 0, s>>>(BD, (int)N, (int)nch, betaTc,
+                                                                      gsumm, gin);
+    st = mmb_launch_status();
+    if (st != MMB_OK) return st;
+    p.gstate_in = gin;
+    p.tchunk = tc;
+    p.nz = (int)nch;
     return launch(desc, p, MM_BWD, s);
 }
 
@@ -226,11 +401,21 @@ static dim3 carry_grid(const CarryArgs& a) {
 
 using namespace mmb;
 
+extern "C" size_t mmb_mmscan_workspace_floats(const mmb_mmscan_desc* desc) {
+    if (!desc || desc->batch <= 0 || desc->seqlen <= 0 || desc->dim <= 0 || desc->dstate <= 0)
+        return 0;
+    return (size_t)(ckpt_floats(desc->batch, desc->seqlen, desc->dim, desc->dstate) +
+                    chunk_floats(desc));
+}
+
 extern "C" size_t mmb_mmscan_ckpt_floats(int64_t batch, int64_t seqlen, int64_t dim,
                                          int64_t dstate) {
-    if (batch <= 0 || seqlen <= 0 || dim <= 0 || dstate <= 0) return 0;
-    const int64_t K = (seqlen + MM_CK - 1) / MM_CK;
-    return (size_t)(batch * K * dim * dstate * 2);
+    mmb_mmscan_desc d{};
+    d.batch = batch;
+    d.seqlen = seqlen;
+    d.dim = dim;
+    d.dstate = dstate;
+    return mmb_mmscan_workspace_floats(&d);
 }
 
 extern "C" int mmb_mmscan_fwd(const mmb_mmscan_desc* desc, const float* x, const float* delta,
@@ -248,7 +433,7 @@ extern "C" int mmb_mmscan_fwd(const mmb_mmscan_desc* desc, const float* x, const
 
 extern "C" int mmb_mmscan_bwd(const mmb_mmscan_desc* desc, const float* x, const float* delta,
                               const float* A, const float* B, const float* C, const float* D,
-                              const float* z, const float* delta_bias, const float* ckpt,
+                              const float* z, const float* delta_bias, float* ckpt,
                               const float* dout, float* dx, float* ddelta, float* dA, float* dB,
                               float* dC, float* dD, float* dz, float* ddelta_bias,
                               mmb_stream_t stream) {
@@ -256,7 +441,7 @@ extern "C" int mmb_mmscan_bwd(const mmb_mmscan_desc* desc, const float* x, const
     if (desc && desc->dtype != MMB_F32) return MMB_ERR_UNSUPPORTED;
     mmb_mmscan_tensors t{};
     t.x = x; t.delta = delta; t.z = z; t.B = B; t.C = C; t.A = A; t.D = D; t.delta_bias = delta_bias;
-    t.ckpt = const_cast<float*>(ckpt);
+    t.ckpt = ckpt;
     t.dout = dout;
     t.dx = dx; t.ddelta = ddelta; t.dz = dz;
     t.dA = dA; t.dB = dB; t.dC = dC; t.dD = dD; t.ddelta_bias = ddelta_bias;

@@ -224,7 +224,39 @@ struct MMParams {
     float* gstate_out;       // (Bsz, D, 2, N): a gh | gv leaving the first step
     void *dx, *ddelta, *dz;
     float *dA, *dB, *dC, *dD, *ddbias;
+    // Time chunks: CTA z covers steps [c T_c, min(L, (c + 1) T_c)), c = z + zoff,
+    // T_c = tchunk (a multiple of MM_T; = L when the sequence is not split).
+    // state_in, summary, gstate_in, state_out, gstate_out are indexed by chunk:
+    // record ((c Bsz + b) D + d).
+    int64_t tchunk;
+    int zoff;
+    int nz;       // time chunks in this launch (grid z)
+    int bsum_pq;  // backward summary also writes the chunk's (P, Q')
 };
+
+// Steps [tb, te) of this CTA's time chunk and its record index for channel d.
+struct MMRange {
+    int64_t tb, te, rec;
+    int cb, ce;  // staged chunks [cb, ce)
+};
+// TCH false: the whole sequence (a kernel built for calls that do not split).
+template <bool TCH = true>
+__device__ __forceinline__ MMRange mm_range(const MMParams& p, int64_t b, int64_t d) {
+    MMRange r;
+    if constexpr (TCH) {
+        const int64_t c = (int64_t)blockIdx.z + p.zoff;
+        r.tb = c * p.tchunk;
+        r.te = min64(p.L, r.tb + p.tchunk);
+        r.rec = (c * p.Bsz + b) * p.D + d;
+    } else {
+        r.tb = 0;
+        r.te = p.L;
+        r.rec = b * p.D + d;
+    }
+    r.cb = (int)(r.tb / MM_T);
+    r.ce = (int)((r.te + MM_T - 1) / MM_T);
+    return r;
+}
 
 // Checkpoints: record (b, window k, channel d) of 2N floats at
 // ((b K + k) D + d) 2N, K = ceil(L / 8); lane ng's [h(NP) | v(NP)] at ng * 2 * NP.
@@ -362,7 +394,7 @@ __device__ __forceinline__ void mm_pipe_init(uint64_t* bars, bool tma) {
 // ---------------------------------------------------------------------------
 // forward (SUMM: the segment summary instead -- no C, z, y or checkpoints)
 // ---------------------------------------------------------------------------
-template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, bool SUMM, int NT>
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, bool SUMM, int NT, bool TCH>
 __global__ void __launch_bounds__(NT)
     mmscan_fwd_kernel(const MMParams p, const __grid_constant__ MMTmaps tmaps) {
     using Cf = MMCfg<N, NP, NT>;
@@ -387,6 +419,8 @@ __global__ void __launch_bounds__(NT)
     const int64_t d = d0 + dl;
     const bool dvalid = d < p.D;
     stg.dcols = (int)min64(DT, p.D - d0);
+    const MMRange rg = mm_range<TCH>(p, b, d);
+    const int64_t te = rg.te;
     const ET* gx = static_cast<const ET*>(p.x);
     const ET* gdl = static_cast<const ET*>(p.delta);
     const ET* gz = static_cast<const ET*>(p.z);
@@ -405,7 +439,7 @@ __global__ void __launch_bounds__(NT)
         }
     }
     if (!SUMM && p.state_in && dvalid) {
-        const float* s = p.state_in + (b * p.D + d) * (2 * N) + ng * NP;
+        const float* s = p.state_in + rg.rec * (2 * N) + ng * NP;
         ld_pairs_g<NP>(s, h);
         ld_pairs_g<NP>(s + N, v);
     }
@@ -413,21 +447,22 @@ __global__ void __launch_bounds__(NT)
     // checkpoint of block 0 of this thread; the next block's is ck_stride further
     const int64_t ck_stride = p.D * (2 * N);
     const bool has_ck = p.ckpt != nullptr;
-    int64_t ckoff = (b * ((p.L + MM_CK - 1) / MM_CK) * p.D + d) * (2 * N) + ng * 2 * NP;
+    int64_t ckoff =
+        ((b * ((p.L + MM_CK - 1) / MM_CK) + rg.tb / MM_CK) * p.D + d) * (2 * N) + ng * 2 * NP;
     const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
     const float Dv = (p.Dskip && dvalid) ? p.Dskip[d] : 0.f;
     const float alpha = p.alpha;
     const float2 beta2 = f2(p.beta);
-    const int nchunks = (int)((p.L + T - 1) / T);
+    const int nchunks = rg.ce - rg.cb;
     // state before a last, partial 8-step block (exact end state: replayed below)
     const bool want_end = SUMM || p.state_out != nullptr;
     int64_t tail_t = -1;
     float2 hs[NP2], vs[NP2], Ps[NP2], Qs[NP2];
     float bps = 1.f;
 
-    auto stage = [&](int slot, int c) {
-        const int64_t t0 = (int64_t)c * T;
-        const int rv = (int)min64(T, p.L - t0);
+    auto stage = [&](int slot, int ci) {
+        const int64_t t0 = (int64_t)(rg.cb + ci) * T;
+        const int rv = (int)min64(T, te - t0);
         stg.begin(slot, HAS_Z ? 3 : 2, SUMM ? 1 : 2);
         stg.tile_d(slot, 0, TM_X, d0, t0, b, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
         stg.tile_d(slot, 1, TM_DELTA, d0, t0, b, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1],
@@ -474,7 +509,7 @@ __global__ void __launch_bounds__(NT)
         const float* sz = st + 2 * Cf::TR;
         const float* sB = st + 3 * Cf::TR;
         const float* sC = sB + Cf::TN;
-        const int64_t t0 = (int64_t)c * T;
+        const int64_t t0 = (int64_t)(rg.cb + c) * T;
 
         // The chunk's blocks.  A whole chunk (all T steps inside the sequence)
         // runs its blocks with no branch between them, so the compiler can
@@ -488,8 +523,8 @@ __global__ void __launch_bounds__(NT)
             for (int k = 0; k < NBLK; ++k) {
                 const int64_t tb = t0 + k * MM_CK;
                 if (!WHOLE) {
-                    if (tb >= p.L) break;
-                    if (want_end && tb + MM_CK > p.L) {
+                    if (tb >= te) break;
+                    if (want_end && tb + MM_CK > te) {
                         tail_t = tb;
 #pragma unroll
                         for (int j = 0; j < NP2; ++j) {
@@ -556,7 +591,7 @@ __global__ void __launch_bounds__(NT)
                             const float zv = sz[Cf::dix(tt, dl)];
                             o *= zv * sigmoid_f(zv);
                         }
-                        if (item_lane && dvalid && (WHOLE || gt < p.L))
+                        if (item_lane && dvalid && (WHOLE || gt < te))
                             E::store(gout, (b * p.L + gt) * p.D + d, o);
                     }
                 }
@@ -570,7 +605,7 @@ __global__ void __launch_bounds__(NT)
                 }
             }
         };
-        if (t0 + T <= p.L)
+        if (t0 + T <= te)
             blocks(std::true_type{});
         else
             blocks(std::false_type{});
@@ -586,8 +621,8 @@ __global__ void __launch_bounds__(NT)
             h[j] = hs[j]; v[j] = vs[j]; Pp[j] = Ps[j]; Qp[j] = Qs[j];
         }
         bpow = bps;
-        const int64_t t0 = (int64_t)(nchunks - 1) * T;
-        for (int64_t t = tail_t; t < p.L; ++t) {
+        const int64_t t0 = (int64_t)(rg.ce - 1) * T;
+        for (int64_t t = tail_t; t < te; ++t) {
             const int tt = (int)(t - t0);
             const float r = st[Cf::TR + Cf::dix(tt, dl)] + bias_d;
             const float dt = SOFTPLUS ? softplus_f(r) : r;
@@ -609,13 +644,13 @@ __global__ void __launch_bounds__(NT)
         }
     }
     if (SUMM) {
-        float* o = p.summary + (b * p.D + d) * (4 * N) + ng * NP;
+        float* o = p.summary + rg.rec * (4 * N) + ng * NP;
         st_pairs_g<NP>(o, h);
         st_pairs_g<NP>(o + N, v);
         st_pairs_g<NP>(o + 2 * N, Pp);
         st_pairs_g<NP>(o + 3 * N, Qp);
     } else {
-        float* o = p.state_out + (b * p.D + d) * (2 * N) + ng * NP;
+        float* o = p.state_out + rg.rec * (2 * N) + ng * NP;
         st_pairs_g<NP>(o, h);
         st_pairs_g<NP>(o + N, v);
     }
@@ -670,6 +705,8 @@ __global__ void __launch_bounds__(NT, 1)
     const int64_t d = d0 + dl;
     const bool dvalid = d < p.D;
     stg.dcols = (int)min64(DT, p.D - d0);
+    const MMRange rg = mm_range(p, b, d);
+    const int64_t te = rg.te;
     const int swz_units = (dl & 1) ? G : 0;
     const ET* gx = static_cast<const ET*>(p.x);
     const ET* gdl = static_cast<const ET*>(p.delta);
@@ -693,7 +730,7 @@ __global__ void __launch_bounds__(NT, 1)
     if (p.gstate_in && dvalid) {
         // the pair arriving from the step after the sequence enters as
         // gh = a_L gh_L with a unit factor
-        const float* s = p.gstate_in + (b * p.D + d) * (2 * N) + ng * NP;
+        const float* s = p.gstate_in + rg.rec * (2 * N) + ng * NP;
         ld_pairs_g<NP>(s, gh);
         ld_pairs_g<NP>(s + N, gv);
 #pragma unroll
@@ -704,7 +741,7 @@ __global__ void __launch_bounds__(NT, 1)
     const float alpha = p.alpha;
     const float2 beta2 = f2(p.beta);
     float accD = 0.f, accBias = 0.f;
-    const int nchunks = (int)((p.L + T - 1) / T);
+    const int nchunks = rg.ce - rg.cb;
     float2 nck_h[NP2], nck_v[NP2];  // checkpoint of the next window to process
 #pragma unroll
     for (int j = 0; j < NP2; ++j) nck_h[j] = nck_v[j] = f2(0.f);
@@ -712,15 +749,16 @@ __global__ void __launch_bounds__(NT, 1)
     // checkpoint (starting at the last one), one stride back per load
     const int64_t ck_stride = p.D * (2 * N);
     const int64_t nck = (p.L + MM_CK - 1) / MM_CK;
-    const float* ckp = p.ckpt_in + ((b * nck + nck - 1) * p.D + d) * (2 * N) + ng * 2 * NP;
+    const float* ckp =
+        p.ckpt_in + ((b * nck + (te - 1) / MM_CK) * p.D + d) * (2 * N) + ng * 2 * NP;
     auto ck_next = [&]() {
         if (dvalid) ckpt_load<NP>(ckp, nck_h, nck_v);
         ckp -= ck_stride;
     };
 
     auto stage = [&](int slot, int c) {
-        const int64_t t0 = (int64_t)c * T;
-        const int rv = (int)min64(T, p.L - t0);
+        const int64_t t0 = (int64_t)(rg.cb + c) * T;
+        const int rv = (int)min64(T, te - t0);
         stg.begin(slot, HAS_Z ? 4 : 3, 2);
         stg.tile_d(slot, 0, TM_X, d0, t0, b, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
         stg.tile_d(slot, 1, TM_DELTA, d0, t0, b, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1],
@@ -756,8 +794,8 @@ __global__ void __launch_bounds__(NT, 1)
         const float* sdo = st + 3 * TR;
         const float* sB = st + 4 * TR;
         const float* sC = sB + Cf::TN;
-        const int64_t t0 = (int64_t)c * T;
-        const int Lc = (int)min64(T, p.L - t0);
+        const int64_t t0 = (int64_t)(rg.cb + c) * T;
+        const int Lc = (int)min64(T, te - t0);
 
         for (int w = (Lc - 1) / MM_CK; w >= 0; --w) {
             const int w0 = w * MM_CK;
@@ -769,7 +807,7 @@ __global__ void __launch_bounds__(NT, 1)
                 h[j] = nck_h[j];
                 v[j] = nck_v[j];
             }
-            if (t0 + w0 > 0) ck_next();
+            if (t0 + w0 > rg.tb) ck_next();
             // this lane's items: dt, alpha*dt*x, dy = dout*silu(z), and the gate's
             // dz / (y + D x) = dout * sigmoid(z) * (1 + z (1 - sigmoid(z)))
             float xi[IPL], ri[IPL], wi[IPL], dti[IPL], dtxi[IPL], dyi[IPL], gzi[IPL];
@@ -878,7 +916,7 @@ __global__ void __launch_bounds__(NT, 1)
                 const int tt = w0 + ibase + i;
                 const int64_t gt = t0 + tt;
                 const int64_t gi = (b * p.L + gt) * p.D + d;
-                const bool ok = item_lane && dvalid && gt < p.L;
+                const bool ok = item_lane && dvalid && gt < te;
                 const float SA = sab[2 * i] * MMB_LN2;
                 const float SB = sab[2 * i + 1];
                 const float xv = xi[i];
@@ -928,7 +966,7 @@ __global__ void __launch_bounds__(NT, 1)
                                 make_float4(acc01.x, acc01.y, acc23.x, acc23.y);
                     } else {
                         const int64_t gt = t0 + w0 + s;
-                        if (part == 0 && gt < p.L) {
+                        if (part == 0 && gt < te) {
                             const int col = q * 4;
                             float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
                             red_add_v4(dst, acc01.x, acc01.y, acc23.x, acc23.y);
@@ -967,7 +1005,7 @@ __global__ void __launch_bounds__(NT, 1)
         float2 lam[NP2];
 #pragma unroll
         for (int j = 0; j < NP2; ++j) lam[j] = fmul2(an[j], gh[j]);
-        float* o = p.gstate_out + (b * p.D + d) * (2 * N) + ng * NP;
+        float* o = p.gstate_out + rg.rec * (2 * N) + ng * NP;
         st_pairs_g<NP>(o, lam);
         st_pairs_g<NP>(o + N, gv);
     }
@@ -1019,15 +1057,21 @@ __global__ void __launch_bounds__(MM_NT)
     const int64_t d = d0 + dl;
     const bool dvalid = d < p.D;
     stg.dcols = (int)min64(DT, p.D - d0);
+    const MMRange rg = mm_range(p, b, d);
+    const int64_t te = rg.te;
     const ET* gdl = static_cast<const ET*>(p.delta);
     const ET* gz = static_cast<const ET*>(p.z);
     const ET* gdo = static_cast<const ET*>(p.dout);
     const ET* gC = static_cast<const ET*>(p.Cm);
 
-    float2 A2[NP2], gh[NP2], gv[NP2], an[NP2];
+    // (gq, gw): the same adjoint recursion without dy, from a unit pair
+    // entering after the last step; at the first step it has become (P, Q')
+    float2 A2[NP2], gh[NP2], gv[NP2], an[NP2], gq[NP2], gw[NP2];
+    const bool pq = p.bsum_pq != 0;
 #pragma unroll
     for (int j = 0; j < NP2; ++j) {
-        A2[j] = gh[j] = gv[j] = an[j] = f2(0.f);
+        A2[j] = gh[j] = gv[j] = gw[j] = f2(0.f);
+        an[j] = gq[j] = f2(1.f);
         if (dvalid) {
             const float* Ar = p.A + d * N + ng * NP + 2 * j;
             A2[j] = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
@@ -1035,11 +1079,11 @@ __global__ void __launch_bounds__(MM_NT)
     }
     const float bias_d = (p.dbias && dvalid) ? p.dbias[d] : 0.f;
     const float2 beta2 = f2(p.beta);
-    const int nchunks = (int)((p.L + T - 1) / T);
+    const int nchunks = rg.ce - rg.cb;
 
     auto stage = [&](int slot, int c) {
-        const int64_t t0 = (int64_t)c * T;
-        const int rv = (int)min64(T, p.L - t0);
+        const int64_t t0 = (int64_t)(rg.cb + c) * T;
+        const int rv = (int)min64(T, te - t0);
         stg.begin(slot, HAS_Z ? 3 : 2, 1);
         stg.tile_d(slot, 1, TM_DELTA, d0, t0, b, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1],
                    rv);
@@ -1071,8 +1115,8 @@ __global__ void __launch_bounds__(MM_NT)
         const float* sz = st + 2 * TR;
         const float* sdo = st + 3 * TR;
         const float* sC = st + 4 * TR + Cf::TN;
-        const int64_t t0 = (int64_t)c * T;
-        const int Lc = (int)min64(T, p.L - t0);
+        const int64_t t0 = (int64_t)(rg.cb + c) * T;
+        const int Lc = (int)min64(T, te - t0);
 
         for (int w = (Lc - 1) / MM_CK; w >= 0; --w) {
             const int w0 = w * MM_CK;
@@ -1114,7 +1158,15 @@ __global__ void __launch_bounds__(MM_NT)
                 for (int j = 0; j < NP2; ++j) {
                     gh[j] = ffma2(an[j], gh[j], fmul2(dy2, cq[j]));
                     gv[j] = ffma2(beta2, gv[j], gh[j]);
-                    an[j] = aa[s][j];
+                    // steps past the end (zero dy) leave gh at zero; they keep
+                    // the unit factor and leave the basis run alone
+                    if (w0 + s < Lc) {
+                        if (pq) {
+                            gq[j] = fmul2(an[j], gq[j]);
+                            gw[j] = ffma2(beta2, gw[j], gq[j]);
+                        }
+                        an[j] = aa[s][j];
+                    }
                 }
             }
         }
@@ -1124,9 +1176,15 @@ __global__ void __launch_bounds__(MM_NT)
     float2 lam[NP2];
 #pragma unroll
     for (int j = 0; j < NP2; ++j) lam[j] = fmul2(an[j], gh[j]);
-    float* o = p.summary + (b * p.D + d) * (2 * N) + ng * NP;
+    float* o = p.summary + rg.rec * ((pq ? 4 : 2) * N) + ng * NP;
     st_pairs_g<NP>(o, lam);
     st_pairs_g<NP>(o + N, gv);
+    if (pq) {
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) gq[j] = fmul2(an[j], gq[j]);
+        st_pairs_g<NP>(o + 2 * N, gq);
+        st_pairs_g<NP>(o + 3 * N, gw);
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -1182,18 +1240,28 @@ MMParams mm_launch_params(const MMParams& p0, MMTmaps& tm) {
 constexpr int MM_SMS = 148;
 constexpr int MM_FWD_SMALL_CTAS_PER_SM = 3;
 
-template <int N, int NP, bool SP, bool Z, class E, bool SUMM, int NT>
-int launch_fwd_nt(const MMParams& p0, cudaStream_t stream) {
+template <int N, int NP, bool SP, bool Z, class E, bool SUMM, int NT, bool TCH>
+int launch_fwd_tch(const MMParams& p0, cudaStream_t stream) {
     using Cf = MMCfg<N, NP, NT>;
     const size_t smem = sizeof(float) * MMSmem<N, NP, 3, E::BYTES, NT>::FLOATS + MM_SMEM_ALIGN;
     static int attr_done[MMB_MAX_DEVICES] = {};
-    const int st = mmb_smem_attr(mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM, NT>, smem, attr_done);
+    const int st =
+        mmb_smem_attr(mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM, NT, TCH>, smem, attr_done);
     if (st != MMB_OK) return st;
     MMTmaps tm;
     const MMParams p = mm_launch_params<N, NP, E, NT>(p0, tm);
-    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
-    mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM, NT><<<grid, NT, smem, stream>>>(p, tm);
+    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz, (unsigned)p.nz);
+    mmscan_fwd_kernel<N, NP, SP, Z, E, SUMM, NT, TCH><<<grid, NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
+}
+
+// A separate build of the forward for calls split along time: the one for
+// whole sequences keeps its bounds in the parameter space (the split build
+// measured slower there: 107 -> 124 us per call at B=32 L=1024 D=256).
+template <int N, int NP, bool SP, bool Z, class E, bool SUMM, int NT>
+int launch_fwd_nt(const MMParams& p0, cudaStream_t stream) {
+    if (p0.tchunk < p0.L) return launch_fwd_tch<N, NP, SP, Z, E, SUMM, NT, true>(p0, stream);
+    return launch_fwd_tch<N, NP, SP, Z, E, SUMM, NT, false>(p0, stream);
 }
 
 template <int N, int NP, bool SP, bool Z, class E, bool SUMM>
@@ -1201,7 +1269,7 @@ int launch_fwd_t(const MMParams& p0, cudaStream_t stream) {
     // 32 threads only where a CTA keeps at least 8 channels (32-byte tile rows)
     if constexpr (!SUMM && 32 / (N / NP) >= 8) {
         constexpr int DT128 = MMCfg<N, NP, MM_NT>::DT;
-        const int64_t ctas = (p0.D + DT128 - 1) / DT128 * p0.Bsz;
+        const int64_t ctas = (p0.D + DT128 - 1) / DT128 * p0.Bsz * p0.nz;
         if (ctas < (int64_t)MM_SMS * MM_FWD_SMALL_CTAS_PER_SM)
             return launch_fwd_nt<N, NP, SP, Z, E, SUMM, 32>(p0, stream);
     }
@@ -1222,7 +1290,7 @@ int launch_bwd_t(const MMParams& p0, cudaStream_t stream) {
     if (st != MMB_OK) return st;
     MMTmaps tm;
     const MMParams p = mm_launch_params<N, NP, E, NT>(p0, tm);
-    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
+    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz, (unsigned)p.nz);
     mmscan_bwd_kernel<N, NP, SP, Z, E, NT><<<grid, NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }
@@ -1236,7 +1304,7 @@ int launch_bwd_summary_t(const MMParams& p0, cudaStream_t stream) {
     if (st != MMB_OK) return st;
     MMTmaps tm;
     const MMParams p = mm_launch_params<N, NP, E>(p0, tm);
-    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz);
+    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz, (unsigned)p.nz);
     mmscan_bwd_summary_kernel<N, NP, SP, Z, E><<<grid, MM_NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }

@@ -69,7 +69,7 @@ class ScanCall:
     fp32 parameters, d_state padded to a compiled size, descriptor built."""
 
     def __init__(self, x, delta, A, B, C, D=None, z=None, delta_bias=None,
-                 delta_softplus=False, beta=0.6, alpha=1.0):
+                 delta_softplus=False, beta=0.6, alpha=1.0, time_chunk=0):
         _lib.require_cuda(x, delta, A, B, C, D, z, delta_bias)
         self.N0 = A.shape[1]
         N = _padded_state(self.N0)
@@ -110,6 +110,7 @@ class ScanCall:
         d.beta, d.alpha = self.beta, self.alpha
         d.delta_softplus = 1 if delta_softplus else 0
         d.dtype = _lib.MMB_BF16 if bf16 else _lib.MMB_F32
+        d.time_chunk = int(time_chunk)
         self.desc = d
 
     @property
@@ -141,8 +142,8 @@ class ScanCall:
         out = torch.empty(self.shape, device=self.device, dtype=self.adtype)
         ckpt = None
         if need_ckpt:
-            ckpt = torch.empty(lib.mmb_mmscan_ckpt_floats(Bsz, L, Dm, self.N), device=self.device,
-                               dtype=torch.float32)
+            ckpt = torch.empty(lib.mmb_mmscan_workspace_floats(ctypes.byref(self.desc)),
+                               device=self.device, dtype=torch.float32)
         state_out = torch.empty(self.state_shape(), device=self.device) if want_state else None
         t = self.tensors(out=out, ckpt=ckpt, state_in=state_in, state_out=state_out)
         self._run("mmb_mmscan_forward", "mmb_mmscan_forward", ctypes.byref(t))
@@ -192,8 +193,10 @@ def _cast_like(g, ref):
 
 class SelectiveScanMomentumFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, delta, A, B, C, D, z, delta_bias, delta_softplus, beta, alpha):
-        call = ScanCall(x, delta, A, B, C, D, z, delta_bias, delta_softplus, beta, alpha)
+    def forward(ctx, x, delta, A, B, C, D, z, delta_bias, delta_softplus, beta, alpha,
+                time_chunk=0):
+        call = ScanCall(x, delta, A, B, C, D, z, delta_bias, delta_softplus, beta, alpha,
+                        time_chunk)
         need_grad = any(ctx.needs_input_grad[:8])
         out, ckpt, _ = call.forward(need_grad)
         ctx.call, ctx.ckpt = call, ckpt
@@ -212,14 +215,17 @@ class SelectiveScanMomentumFn(torch.autograd.Function):
             res.append((g if dt is None or g.dtype == dt else g.to(dt)) if need and g is not None
                        else None)
         ctx.call = ctx.ckpt = None
-        return (*res, None, None, None)
+        return (*res, None, None, None, None)
 
 
 def selective_scan_momentum_fn(x, delta, A, B, C, D=None, z=None, delta_bias=None,
-                               delta_softplus=False, beta=0.6, alpha=1.0):
+                               delta_softplus=False, beta=0.6, alpha=1.0, time_chunk=0):
     """Fused momentum selective scan; see the module docstring.  All tensors on one
     CUDA device; x, delta, z (batch, seqlen, dim); A (dim, d_state); B, C
     (batch, seqlen, d_state); D, delta_bias (dim).  Returns (batch, seqlen, dim)
-    in the activation dtype (bf16 when x, delta, z, B, C are all bf16, else fp32)."""
+    in the activation dtype (bf16 when x, delta, z, B, C are all bf16, else fp32).
+    time_chunk: steps per time chunk scanned by separate CTAs (0: the library
+    splits short batches of long sequences on its own; < 0: never split)."""
     return SelectiveScanMomentumFn.apply(x, delta, A, B, C, D, z, delta_bias,
-                                         bool(delta_softplus), float(beta), float(alpha))
+                                         bool(delta_softplus), float(beta), float(alpha),
+                                         int(time_chunk))

@@ -39,7 +39,7 @@ def test_library_exports_every_declared_symbol():
 
 def test_status_strings_and_version():
     lib = _lib.load()
-    assert lib.mmb_abi_version() >= 1
+    assert lib.mmb_abi_version() >= 3
     assert lib.mmb_status_string(0) == b"ok"
     for code in range(1, 8):
         assert lib.mmb_status_string(code) != b"unknown status"
@@ -48,10 +48,31 @@ def test_status_strings_and_version():
 
 def test_ckpt_size_formula():
     lib = _lib.load()
-    # batch * ceil(L / 8) * dim * dstate * 2
+    # batch * ceil(L / 8) * dim * dstate * 2 when the call does not split along time
     assert lib.mmb_mmscan_ckpt_floats(2, 256, 64, 16) == 2 * 32 * 64 * 16 * 2
-    assert lib.mmb_mmscan_ckpt_floats(1, 300, 16, 8) == 1 * 38 * 16 * 8 * 2
+    assert lib.mmb_mmscan_ckpt_floats(32, 1024, 256, 16) == 32 * 128 * 256 * 16 * 2
     assert lib.mmb_mmscan_ckpt_floats(0, 10, 10, 16) == 0
+    # one sequence of 16 channels gives the GPU one warp: the library splits 300
+    # steps into chunks of 256 and adds chunks * batch * dim * dstate * 6 floats
+    assert lib.mmb_mmscan_ckpt_floats(1, 300, 16, 8) == 1 * 38 * 16 * 8 * 2 + 2 * 16 * 8 * 6
+
+
+def test_workspace_follows_the_time_chunk():
+    lib = _lib.load()
+    d = _desc(shape=(2, 1000, 64, 16))
+    ck = 2 * 125 * 64 * 16 * 2
+    d.time_chunk = -1                      # never split
+    assert lib.mmb_mmscan_workspace_floats(ctypes.byref(d)) == ck
+    d.time_chunk = 100                     # rounded up to 128 steps: 8 chunks
+    assert lib.mmb_mmscan_workspace_floats(ctypes.byref(d)) == ck + 8 * 2 * 64 * 16 * 6
+    d.time_chunk = 1000                    # one chunk
+    assert lib.mmb_mmscan_workspace_floats(ctypes.byref(d)) == ck
+    d.time_chunk = 0                       # automatic: 16 warps -> chunks of 256 steps
+    assert lib.mmb_mmscan_workspace_floats(ctypes.byref(d)) == ck + 4 * 2 * 64 * 16 * 6
+    assert lib.mmb_mmscan_workspace_floats(ctypes.byref(d)) == lib.mmb_mmscan_ckpt_floats(
+        2, 1000, 64, 16)
+    assert lib.mmb_mmscan_workspace_floats(None) == 0
+    assert ctypes.sizeof(_lib.MMScanDesc) == 136
 
 
 def _desc(**kw):
