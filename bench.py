@@ -18,11 +18,13 @@ Extra keys of the same line (each with its own roofline):
   * ``long_seq``:   B=8 L=65536 D=2048 N=16 in bf16, split along time over the
                     ranks (segment summaries all-gathered over NCCL);
   * ``linoss``:     the LinOSS layer scan, IM and IMEX, B=16 L=4096 P=256;
+  * ``linoss_layer``: the whole LinOSS layer (tensor-core contractions + scan)
+                    at H=128, with the cuBLAS-contraction layer's time beside;
   * ``rows``:       the row-form and PScan-layout scans at the stack's size.
 On N > 1 GPUs only ``long_seq`` runs beside the default line.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
-                    [--workload classifier|stack|chunks|long|linoss|rows] [--no-extras]
+                    [--workload classifier|stack|chunks|long|linoss|linoss_layer|rows] [--no-extras]
 
 Rank 0 prints ONE JSON line.  ``--impl reference`` times the CPU restatement
 of the reference algorithm (oracle/, fp32 variant, all host threads) on a
@@ -859,6 +861,81 @@ def run_linoss(ctx, steps):
     }
 
 
+def run_linoss_layer(ctx, steps):
+    """The whole LinOSSLayer (LinOSS_pytorch.py:258-312) forward + backward, IM and
+    IMEX, at H=128 P=256 B=16 L=4096: Bu = B u and y = Re(C x2) + D u with their
+    gradients on the tensor cores (tcgen05, 3 x tf32) around the LinOSS scan
+    kernels.  Beside it, the same layer with the contractions as fp32 cuBLAS
+    GEMMs (torch.matmul; the reference's einsums) around the same scan.
+    Elements = B L P oscillator steps per discretisation."""
+    import torch
+
+    import momentummamba_b200.LinOSS_pytorch as lp
+    from momentummamba_b200.scan2 import linoss_scan
+
+    args, dev, world = ctx.args, ctx.dev, ctx.world
+    Bsz, L, P, H = LINOSS["batch"], LINOSS["seqlen"], LINOSS["osc"], 128
+    torch.manual_seed(11 + ctx.rank)
+    layers = [lp.LinOSSLayer(P, H, d).to(dev) for d in ("IM", "IMEX")]
+    u = torch.randn(Bsz, L, H, device=dev, requires_grad=True)
+    gy = torch.randn(Bsz, L, H, device=dev)
+
+    def cublas_layer(layer, x):
+        A = torch.relu(layer.A_diag)
+        s = torch.sigmoid(layer.steps)
+        bu = torch.complex(x @ layer.B_real.t(), x @ layer.B_imag.t())
+        x2 = linoss_scan(layer.discretization, A, s, bu)
+        return x2.real @ layer.C_real.t() - x2.imag @ layer.C_imag.t() + x * layer.D
+
+    def step_tc():
+        for ly in layers:
+            ly(u).backward(gy)
+
+    def step_cublas():
+        for ly in layers:
+            cublas_layer(ly, u).backward(gy)
+
+    for _ in range(max(3, args.warmup)):
+        step_tc()
+        step_cublas()
+    torch.cuda.synchronize()
+    ms, clocks = timed_region(ctx, step_tc, steps)
+    ms_cu, _ = timed_region(ctx, step_cublas, max(3, steps // 4))
+    ms_cu *= steps / max(3, steps // 4)
+    # one of the four tensor-core GEMM shapes alone: Bu = u Bm^T (M = B L, N = 2P, K = H)
+    from momentummamba_b200.tc_gemm import gemm_nt
+    u2 = u.detach().reshape(Bsz * L, H)
+    Bm = torch.randn(2 * P, H, device=dev)
+    t = launch_times((("tc_gemm Bu", lambda: gemm_nt(u2, Bm)),))
+    del layers, u, gy, u2, Bm
+    torch.cuda.empty_cache()
+    if ctx.rank != 0:
+        return None
+    elems = Bsz * L * P
+    peak, peak_kind = load_peaks()
+    gemm_b = Bsz * L * (H + 2 * P) * 4            # read u, write Bu
+    achieved = gemm_b / (t["tc_gemm Bu"] / 1e3) / 1e9
+    return {
+        "metric": METRIC, "value": job_rate(2 * elems * steps, world, ms), "unit": UNIT,
+        "n_gpus": world, "steps": steps, "warmup": args.warmup,
+        "ms_per_step": ms / steps, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "LinOSSLayer forward + backward (GEMMs + scan), IM and IMEX: "
+                               "B=16 L=4096 H=128 P=256, u ~ N(0,1), module init",
+                   "parallelism": f"batch-sharded x{world}", "launch": "eager (autograd)",
+                   "l2": "inputs larger than L2 (Bu, x2 134 MB each)"},
+        "cublas_contractions_ms_per_step": ms_cu / steps,
+        "roofline": {"kernel": "tc_gemm_kernel (Bu = u Bm^T, M=65536 N=512 K=128)",
+                     "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": achieved / peak,
+                     "algorithmic_bytes": gemm_b, "ms_per_launch": t["tc_gemm Bu"],
+                     "traffic": None},
+        # per discretisation: forward 2 GEMMs + 3 scan launches, backward 4 GEMMs + 4
+        "gpu_launches": 26 * steps,
+        "clocks": clocks,
+    }
+
+
 def linoss_cpu_baseline(budget_s=5.0):
     """The fp32 oracle's 2x2 scan (forward + backward) on the host cores, for one
     sequence of the LinOSS workload (IM transition)."""
@@ -987,8 +1064,8 @@ def summary(line):
     if line is None:
         return None
     keep = ("value", "unit", "n_gpus", "steps", "ms_per_step", "scaling", "dtype", "config",
-            "roofline", "kernels", "time_chunks", "unsplit", "phases_ms", "gpu_launches",
-            "clocks", "cpu_baseline")
+            "roofline", "kernels", "time_chunks", "unsplit", "cublas_contractions_ms_per_step",
+            "phases_ms", "gpu_launches", "clocks", "cpu_baseline")
     return {k: line[k] for k in keep if k in line}
 
 
@@ -1004,7 +1081,7 @@ def main():
                     help="default workload only (no extra keys)")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--workload", choices=["classifier", "stack", "chunks", "long", "linoss",
-                                           "rows"],
+                                           "linoss_layer", "rows"],
                     default="classifier",
                     help="classifier: the 6-layer momentum-Mamba classifier scan, B=256 T=300 "
                          "D=512 split over the ranks (the benchmark line, with the other "
@@ -1046,6 +1123,7 @@ def main():
                                                           with_e2e=False, with_cpu=False,
                                                           name="time_chunks"))
                 extras["linoss"] = summary(run_linoss(ctx, 2 * K))
+                extras["linoss_layer"] = summary(run_linoss_layer(ctx, max(3, K // 4)))
                 extras["rows"] = summary(run_rows(ctx, max(3, K // 4)))
             if line is not None:
                 line["extras"] = extras
@@ -1060,6 +1138,8 @@ def main():
         line = run_long(ctx, K)
     elif args.workload == "linoss":
         line = run_linoss(ctx, K)
+    elif args.workload == "linoss_layer":
+        line = run_linoss_layer(ctx, K)
     else:
         line = run_rows(ctx, K)
     ctx.close()

@@ -390,6 +390,29 @@ int mmb_scan2_fwd_noalloc(int64_t batch, int64_t L, int64_t P, int32_t complex_f
                           mmb_stream_t stream);
 
 /* =========================================================================
+ * fp32-accurate GEMM on the tensor cores (tcgen05, 3 x tf32 split), for the
+ * dense contractions of the LinOSS layer -- complex_matmul_real_input and
+ * complex_matmul_complex_state (LinOSS_pytorch.py:135-150), as real GEMMs on
+ * interleaved complex data, and their gradients:
+ *
+ *   C[m, n] (= or +=) sum_k A(m, k) B(n, k)  [+ evec[n] * E[m, n]]
+ *
+ * A(m, k) = A[m * lda + k] (a_mn == 0, K-major) or A[k * lda + m] (a_mn != 0);
+ * B(n, k) = B[n * ldb + k] (b_mn == 0) or B[k * ldb + n] (b_mn != 0);
+ * C and E row-major with ldc, lde >= N.  A, B 16-byte aligned, lda and ldb
+ * multiples of 4.  Each operand is split into a tf32 high part and an fp32
+ * remainder; the three significant partial products are accumulated in fp32
+ * (error within a few fp32 ulps of the products).  accumulate != 0 adds into
+ * C with vector reductions (C cleared by the caller); splits > 1 cuts K into
+ * that many slices, one CTA per slice and tile (needs accumulate).  E, evec
+ * nullable (both or neither).
+ * ========================================================================= */
+int mmb_gemm_f32(int32_t a_mn, int32_t b_mn, int64_t M, int64_t N, int64_t K, const float* A,
+                 int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                 const float* E, int64_t lde, const float* evec, int32_t accumulate,
+                 int32_t splits, mmb_stream_t stream);
+
+/* =========================================================================
  * LinOSS layer scan with a time-invariant transition per oscillator p -- the
  * scan inside apply_linoss_im_complex / apply_linoss_imex_complex
  * (LinOSS_pytorch.py:153-239), batched:

@@ -1,11 +1,15 @@
-"""LinOSS on the sm_100a scan kernels -- drop-in for the reference's LinOSS_pytorch.py.
+"""LinOSS on the sm_100a kernels -- drop-in for the reference's LinOSS_pytorch.py.
 
 Same names, module tree and parameter names.  The scan inside
 apply_linoss_im_complex / apply_linoss_imex_complex runs on the fused LinOSS
 kernel (transition and input scale built in registers per oscillator, chunked
-over time, batched over sequences), so LinOSSLayer needs no vmap; the complex
-GEMMs around it (Bu = B u, y = Re(C x2)) stay with cuBLAS.
-``parallel_scan_batched`` is the generic 2x2 scan kernel on one sequence.
+over time, batched over sequences), so LinOSSLayer needs no vmap.  The complex
+GEMMs around it (Bu = B u, y = Re(C x2) + D u, and their gradients) run on the
+tensor cores (tc_gemm: tcgen05 with a 3 x tf32 split, fp32-grade accuracy) as
+real GEMMs on interleaved complex data, so Bu comes out in the scan's layout
+and x2 goes in as it is: no re/im copies, the feedthrough D u is the y GEMM's
+epilogue.  ``parallel_scan_batched`` is the generic 2x2 scan kernel on one
+sequence.
 """
 from __future__ import annotations
 
@@ -16,7 +20,9 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from .scan2 import linoss_scan, scan2
+from . import _lib
+from .scan2 import _DISC, _real_view, linoss_scan, scan2
+from .tc_gemm import gemm_nt, gemm_tn
 
 VMAP_AVAILABLE = True
 
@@ -74,12 +80,71 @@ def complex_matmul_complex_state(C_real, C_imag, state_real, state_imag):
     return state_real @ C_real.t() - state_imag @ C_imag.t()
 
 
-def _apply(disc, A_diag, B_real, B_imag, C_real, C_imag, input_sequence, step):
+class LinOSSLayerFn(torch.autograd.Function):
+    """y = Re(C x2) + D u with x2 the LinOSS scan of F(B u) (LinOSS_pytorch.py:153-239,
+    :306-312), on interleaved complex data: Bm = [B_re; B_im] rows interleaved
+    (2P, H), Cc[h, (p, re | im)] = (C_re, -C_im)[h, p] (H, 2P), so that
+    Bu = u Bm^T comes out as complex (B, L, P) and y = x2 Cc^T + D u reads x2 as
+    it is.  Gradients: dx2 = dy Cc, dBu from the scan's adjoint, du = dBu Bm +
+    D dy, dBm = dBu^T u, dCc = dy^T x2, dD = sum dy u."""
+
+    @staticmethod
+    def forward(ctx, disc, A_diag, step, B_real, B_imag, C_real, C_imag, D, u):
+        _lib.require_cuda(A_diag, step, B_real, B_imag, C_real, C_imag, D, u)
+        if disc not in _DISC:
+            raise ValueError(f"Discretization type {disc} not implemented")
+        Bsz, L, H = u.shape
+        P = A_diag.shape[0]
+        u2 = u.reshape(Bsz * L, H).float().contiguous()
+        Bm = torch.stack([B_real.float(), B_imag.float()], dim=1).reshape(2 * P, H)
+        Cc = torch.stack([C_real.float(), -C_imag.float()], dim=2).reshape(H, 2 * P)
+        Bu = gemm_nt(u2, Bm).view(Bsz, L, P, 2)
+        A, s = A_diag.float().contiguous(), step.float().contiguous()
+        lib = _lib.load()
+        x2 = torch.empty_like(Bu)
+        work = torch.empty(lib.mmb_linoss_work_floats(Bsz, L, P), device=u.device)
+        with torch.cuda.device(u.device):
+            st = lib.mmb_linoss_fwd(_DISC[disc], Bsz, L, P, _lib.ptr(A), _lib.ptr(s),
+                                    _lib.ptr(Bu), _lib.ptr(x2), _lib.ptr(work),
+                                    _lib.stream_of(u))
+        _lib.check(st, "mmb_linoss_fwd")
+        Dv = D.float().contiguous() if D is not None else None
+        y = gemm_nt(x2.view(Bsz * L, 2 * P), Cc, E=u2 if Dv is not None else None, evec=Dv)
+        ctx.save_for_backward(A, s, Bm, Cc, u2, Bu, x2, work, Dv)
+        ctx.disc, ctx.has_d, ctx.shape = disc, Dv is not None, (Bsz, L, H, P)
+        return y.view(Bsz, L, H)
+
+    @staticmethod
+    def backward(ctx, dy):
+        A, s, Bm, Cc, u2, Bu, x2, work, Dv = ctx.saved_tensors
+        Bsz, L, H, P = ctx.shape
+        dy2 = dy.reshape(Bsz * L, H).float().contiguous()
+        dx2 = gemm_nt(dy2, Cc.t().contiguous())                    # (B L, 2P)
+        lib = _lib.load()
+        dBu = torch.empty_like(Bu)
+        dA = torch.empty_like(A)
+        ds = torch.empty_like(s)
+        with torch.cuda.device(A.device):
+            st = lib.mmb_linoss_bwd(_DISC[ctx.disc], Bsz, L, P, _lib.ptr(A), _lib.ptr(s),
+                                    _lib.ptr(Bu), _lib.ptr(dx2), _lib.ptr(dBu), _lib.ptr(dA),
+                                    _lib.ptr(ds), _lib.ptr(work), _lib.stream_of(A))
+        _lib.check(st, "mmb_linoss_bwd")
+        dBu2 = dBu.view(Bsz * L, 2 * P)
+        du = gemm_nt(dBu2, Bm.t().contiguous(), E=dy2 if ctx.has_d else None,
+                     evec=Dv if ctx.has_d else None)
+        dBm = gemm_tn(dBu2, u2)                                     # (2P, H)
+        dCc = gemm_tn(dy2, x2.view(Bsz * L, 2 * P))                 # (H, 2P)
+        dD = (dy2 * u2).sum(0) if ctx.has_d else None
+        dBm = dBm.view(P, 2, H)
+        dCc = dCc.view(H, P, 2)
+        return (None, dA, ds, dBm[:, 0], dBm[:, 1], dCc[..., 0], -dCc[..., 1], dD,
+                du.view(Bsz, L, H))
+
+
+def _apply(disc, A_diag, B_real, B_imag, C_real, C_imag, input_sequence, step, D=None):
     squeeze = input_sequence.dim() == 2
     u = input_sequence.unsqueeze(0) if squeeze else input_sequence
-    bu_r, bu_i = complex_matmul_real_input(B_real, B_imag, u.float())
-    x2 = linoss_scan(disc, A_diag, step, torch.complex(bu_r, bu_i))
-    y = complex_matmul_complex_state(C_real, C_imag, x2.real, x2.imag)
+    y = LinOSSLayerFn.apply(disc, A_diag, step, B_real, B_imag, C_real, C_imag, D, u)
     return y[0] if squeeze else y
 
 
@@ -112,9 +177,9 @@ class LinOSSLayer(nn.Module):
             raise ValueError(f"Discretization type {self.discretization} not implemented")
         A = F.relu(self.A_diag)
         steps = torch.sigmoid(self.steps)
-        ys = _apply(self.discretization, A, self.B_real, self.B_imag, self.C_real, self.C_imag,
-                    input_sequence, steps)
-        return ys + input_sequence * self.D
+        # the feedthrough D u is the output GEMM's epilogue
+        return _apply(self.discretization, A, self.B_real, self.B_imag, self.C_real, self.C_imag,
+                      input_sequence, steps, D=self.D)
 
 
 class LinOSSBlock(nn.Module):

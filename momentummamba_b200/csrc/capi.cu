@@ -132,7 +132,9 @@ bool mmb_encode_tile_map(CUtensorMap* map, const void* base, int elem_bytes, int
                                    (cuuint64_t)(stride2 * elem_bytes)};
     const cuuint32_t box[3] = {(cuuint32_t)box0, (cuuint32_t)box1, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
-    const CUtensorMapSwizzle sw = swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+    const CUtensorMapSwizzle sw = swizzle_bytes == MMB_SWZ_128B_ATOM32
+                                      ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B
+                                  : swizzle_bytes == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
                                   : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                   : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                                         : CU_TENSOR_MAP_SWIZZLE_NONE;

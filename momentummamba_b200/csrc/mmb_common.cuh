@@ -412,8 +412,11 @@ int* mmb_device_error_flag();
 
 // Encode a 3-D tiled tensor map over dims (dim0 innermost, unit stride; dim1 and
 // dim2 with element strides stride1, stride2) for boxes of box0 x box1 x 1
-// elements of elem_bytes (4: fp32, 2: bf16), swizzle span 0/32/64/128 bytes,
-// out-of-range elements read as zero.  false if the driver refuses.
+// elements of elem_bytes (4: fp32, 2: bf16), swizzle span 0/32/64/128 bytes
+// (16-byte chunks permuted within the span), or MMB_SWZ_128B_ATOM32 (32-byte
+// chunks permuted within 128 bytes), out-of-range elements read as zero.
+// false if the driver refuses.
+constexpr int MMB_SWZ_128B_ATOM32 = 1128;
 bool mmb_encode_tile_map(CUtensorMap* map, const void* base, int elem_bytes, int64_t dim0,
                          int64_t dim1, int64_t dim2, int64_t stride1, int64_t stride2,
                          int box0, int box1, int swizzle_bytes);

@@ -1,0 +1,460 @@
+// fp32-accurate GEMM on the sm_100a tensor cores (tcgen05, TMEM accumulator)
+// for the dense contractions around the LinOSS layer scan.
+//
+//   C[m, n] (= or +=) sum_k A(m, k) B(n, k)  [+ evec[n] * E[m, n]]
+//
+// A and B are fp32 in global memory, each either K-major (row m / n holds the
+// K values contiguously) or MN-major (row k holds the M / N values
+// contiguously).  Accuracy: every operand x is split in shared memory into
+// x_hi = x with its low 13 mantissa bits cleared (exact in tf32) and
+// x_lo = x - x_hi (exact in fp32); the tensor cores accumulate
+// A_hi B_hi + A_hi B_lo + A_lo B_hi in fp32 (kind::tf32), which leaves an
+// error of a few fp32 ulps of the products (the dropped A_lo B_lo term is
+// 2^-22 relative) -- close to a plain fp32 GEMM, unlike one-pass tf32 (2^-11).
+//
+// Tile: 128 x BN (BN = 128 or 256) per CTA, K in steps of 16 (one 64-byte
+// swizzle row of fp32 for K-major operands), two pipeline stages: 48 KB of
+// shared memory per stage at BN = 256, so two CTAs share an SM and one's
+// epilogue overlaps the other's loads (32-value K steps, one CTA per SM,
+// measured 118 us for M=65536 N=512 K=128).  Thread 0 issues the TMA copies
+// (raw fp32 tiles, 128-byte swizzle) and the MMAs; all 128 threads split the
+// landed tiles into hi / lo in place and, at the end, read the accumulator out
+// of TMEM (one row per thread) for the epilogue.  Split-K (grid z) adds its
+// partial tile to C with vector reductions.
+#include "mmb_common.cuh"
+
+namespace mmb {
+
+constexpr int TG_BM = 128;
+constexpr int TG_BK = 16;
+constexpr int TG_NT = 128;
+#ifndef MMB_TG_STAGES
+#define MMB_TG_STAGES 2
+#endif
+#ifndef MMB_TG_BN_MAX
+#define MMB_TG_BN_MAX 256
+#endif
+constexpr int TG_STAGES = MMB_TG_STAGES;
+constexpr uint32_t TG_MASK_HI = 0xffffe000u;  // fp32 bits kept by tf32
+
+// ---------------------------------------------------------------------------
+// tcgen05 / TMEM wrappers (inline PTX)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void tmem_alloc(uint32_t* smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(smem_dst)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// generic-proxy writes to shared memory -> visible to the tensor cores
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::tf32, issued by one thread
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// arrive on `bar` once every MMA this thread issued before has completed
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+            smem_u32(bar))
+        : "memory");
+}
+// 32 consecutive 32-bit columns of this thread's TMEM lane
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+        "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+        "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+          "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+          "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+          "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+          "=r"(r[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+// Shared-memory matrix descriptor (sm_100 layout: start address, leading and
+// stride byte offsets in 16-byte units, version 1 at bit 46, swizzle mode at
+// bits 61-63).
+//   K-major (mode 4, 64-byte swizzle of 16-byte chunks): rows of 64 bytes
+//   (16 K values), 8-row groups `sbo` apart; the leading offset is unused.
+//   MN-major (mode 1, 128-byte swizzle of 32-byte chunks -- the only
+//   MN-major layout tf32 operands take): K-rows of 128 bytes (32 M / N
+//   values), 4-row groups `sbo` apart along K, 32-value M / N blocks `lbo`
+//   apart.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t mode) {
+    return (uint64_t)((saddr >> 4) & 0x3fffu) | ((uint64_t)((lbo >> 4) & 0x3fffu) << 16) |
+           ((uint64_t)((sbo >> 4) & 0x3fffu) << 32) | (1ull << 46) | ((uint64_t)mode << 61);
+}
+
+// Instruction descriptor of kind::tf32 with fp32 accumulation: M = 128, N = n;
+// a_mn / b_mn select MN-major operands.
+__host__ __device__ constexpr uint32_t tf32_idesc(int n, bool a_mn, bool b_mn) {
+    return (1u << 4)                  // D fp32
+           | (2u << 7) | (2u << 10)   // A, B tf32
+           | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
+           ((uint32_t)(n >> 3) << 17) | ((uint32_t)(TG_BM >> 4) << 24);
+}
+
+struct TGParams {
+    int64_t M, N, K, kchunk;  // kchunk: K per grid-z slice (multiple of TG_BK)
+    float* C;
+    int64_t ldc;
+    const float* E;  // nullable epilogue term evec[n] * E[m, n]
+    int64_t lde;
+    const float* evec;
+    int accumulate;  // 1: C += (vector reductions; split-K), 0: C =
+    int tma_c;       // C goes out through 32 x 32 TMA boxes (aligned C)
+    int* err;
+};
+struct TGMaps {
+    CUtensorMap a, b, c;  // c: 32 x 32 boxes of C, 128-byte swizzle (when p.tma_c)
+};
+
+// TMA store / reduce-add of one 32 x 32 box of C from shared memory (bulk group)
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const float* src, int c0,
+                                             int c1, bool add) {
+    if (add)
+        asm volatile(
+            "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group"
+            " [%0, {%1, %2, %3}], [%4];" ::"l"(reinterpret_cast<uint64_t>(map)),
+            "r"(c0), "r"(c1), "r"(0), "r"(smem_u32(src))
+            : "memory");
+    else
+        asm volatile(
+            "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group"
+            " [%0, {%1, %2, %3}], [%4];" ::"l"(reinterpret_cast<uint64_t>(map)),
+            "r"(c0), "r"(c1), "r"(0), "r"(smem_u32(src))
+            : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// wait until at most N bulk groups of this thread still read shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+template <int BN>
+struct TGSmem {
+    static constexpr int A_FLOATS = TG_BM * TG_BK;  // 8 KB
+    static constexpr int B_FLOATS = BN * TG_BK;
+    // per stage: A_hi | A_lo | B_hi | B_lo (each 1024-byte aligned)
+    static constexpr int STAGE = 2 * A_FLOATS + 2 * B_FLOATS;
+    static constexpr size_t BYTES = (size_t)TG_STAGES * STAGE * 4 + 1024;
+};
+
+// Load one 128 x 16 (A) or BN x 16 (B) fp32 tile.  K-major: one box of 16 (K)
+// x rows, 64-byte swizzle.  MN-major: boxes of 32 (M / N) x 16 (K), one per
+// 32-value block, each 2 KB, 32-byte-chunk swizzle.
+template <int ROWS, bool MN>
+__device__ __forceinline__ void tg_load(float* dst, const CUtensorMap* map, int64_t r0, int64_t k0,
+                                        uint64_t* bar) {
+    if constexpr (!MN) {
+        tma_load_3d(dst, map, (int)k0, (int)r0, 0, bar);
+    } else {
+#pragma unroll
+        for (int g = 0; g < ROWS / 32; ++g)
+            tma_load_3d(dst + g * 32 * TG_BK, map, (int)(r0 + 32 * g), (int)k0, 0, bar);
+    }
+}
+
+// Descriptor of K-step kk (8 values of K) of a tile at `base`.
+template <int ROWS, bool MN>
+__device__ __forceinline__ uint64_t tg_desc(const float* base, int kk) {
+    const uint32_t s = smem_u32(base);
+    if constexpr (!MN) return smem_desc(s + kk * 32, 16, 512, 4);
+    else return smem_desc(s + kk * 1024, 32 * TG_BK * 4, 512, 1);
+}
+
+// Split the landed tile in place into hi, and lo into `lo` (same layout).
+template <int FLOATS>
+__device__ __forceinline__ void tg_split(float* hi, float* lo, int tid) {
+#pragma unroll 4
+    for (int i = tid; i < FLOATS / 4; i += TG_NT) {
+        float4 x = reinterpret_cast<float4*>(hi)[i];
+        float4 h, l;
+        h.x = __uint_as_float(__float_as_uint(x.x) & TG_MASK_HI);
+        h.y = __uint_as_float(__float_as_uint(x.y) & TG_MASK_HI);
+        h.z = __uint_as_float(__float_as_uint(x.z) & TG_MASK_HI);
+        h.w = __uint_as_float(__float_as_uint(x.w) & TG_MASK_HI);
+        l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
+        reinterpret_cast<float4*>(hi)[i] = h;
+        reinterpret_cast<float4*>(lo)[i] = l;
+    }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(TG_NT)
+    tc_gemm_kernel(const TGParams p, const __grid_constant__ TGMaps maps) {
+    using Sm = TGSmem<BN>;
+    extern __shared__ float4 tg_smem4[];
+    __shared__ uint64_t tma_bar[TG_STAGES], mma_bar[TG_STAGES];
+    __shared__ uint32_t tmem_base_s;
+    float* smem = reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(tg_smem4) + 1023) & ~(uintptr_t)1023);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int64_t m0 = (int64_t)blockIdx.x * TG_BM;
+    const int64_t n0 = (int64_t)blockIdx.y * BN;
+    const int64_t kb = (int64_t)blockIdx.z * p.kchunk;
+    const int64_t ke = min64(p.K, kb + p.kchunk);
+    const int nk = (int)((ke - kb + TG_BK - 1) / TG_BK);
+    constexpr uint32_t IDESC = tf32_idesc(BN, A_MN, B_MN);
+    constexpr uint32_t TX = (uint32_t)(TG_BM + BN) * TG_BK * 4;
+
+    if (tid == 0) {
+        for (int s = 0; s < TG_STAGES; ++s) {
+            mbar_init(&tma_bar[s], 1);
+            mbar_init(&mma_bar[s], 1);
+        }
+        mbar_fence_init();
+    }
+    if (warp == 0) tmem_alloc(&tmem_base_s, BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    auto a_hi = [&](int s) { return smem + s * Sm::STAGE; };
+    auto a_lo = [&](int s) { return smem + s * Sm::STAGE + Sm::A_FLOATS; };
+    auto b_hi = [&](int s) { return smem + s * Sm::STAGE + 2 * Sm::A_FLOATS; };
+    auto b_lo = [&](int s) { return smem + s * Sm::STAGE + 2 * Sm::A_FLOATS + Sm::B_FLOATS; };
+    auto issue = [&](int i) {  // thread 0: TMA of K-tile i into stage i % 2
+        const int s = i % TG_STAGES;
+        const int64_t k0 = kb + (int64_t)i * TG_BK;
+        mbar_expect_tx(&tma_bar[s], TX);
+        tg_load<TG_BM, A_MN>(a_hi(s), &maps.a, m0, k0, &tma_bar[s]);
+        tg_load<BN, B_MN>(b_hi(s), &maps.b, n0, k0, &tma_bar[s]);
+    };
+
+    bool ok = true;
+    if (tid == 0 && nk > 0) issue(0);
+    for (int i = 0; i < nk; ++i) {
+        const int s = i % TG_STAGES;
+        // thread 0: the next tile goes into the other stage once the MMAs that
+        // read it (tile i - 1) are done
+        if (tid == 0 && i + 1 < nk) {
+            if (i >= 1) ok = mbar_wait_bounded(&mma_bar[(i - 1) % TG_STAGES],
+                                               (uint32_t)(((i - 1) / TG_STAGES) & 1));
+            if (ok) issue(i + 1);
+        }
+        if (ok) ok = mbar_wait_bounded(&tma_bar[s], (uint32_t)((i / TG_STAGES) & 1));
+        if (__syncthreads_or(!ok)) break;
+        tg_split<Sm::A_FLOATS>(a_hi(s), a_lo(s), tid);
+        tg_split<Sm::B_FLOATS>(b_hi(s), b_lo(s), tid);
+        fence_proxy_async_smem();
+        __syncthreads();
+        if (tid == 0) {
+            tc_fence_after();
+#pragma unroll
+            for (int kk = 0; kk < TG_BK / 8; ++kk) {
+                const uint64_t ah = tg_desc<TG_BM, A_MN>(a_hi(s), kk);
+                const uint64_t al = tg_desc<TG_BM, A_MN>(a_lo(s), kk);
+                const uint64_t bh = tg_desc<BN, B_MN>(b_hi(s), kk);
+                const uint64_t bl = tg_desc<BN, B_MN>(b_lo(s), kk);
+                umma_tf32(tmem, ah, bh, IDESC, (i > 0 || kk > 0) ? 1u : 0u);
+                umma_tf32(tmem, ah, bl, IDESC, 1u);
+                umma_tf32(tmem, al, bh, IDESC, 1u);
+            }
+            umma_commit(&mma_bar[s]);
+        }
+    }
+    // the accumulator is complete once the last tile's MMAs are
+    if (ok && nk > 0) {
+        const int l = nk - 1;
+        ok = mbar_wait_bounded(&mma_bar[l % TG_STAGES], (uint32_t)((l / TG_STAGES) & 1));
+    }
+    if (__syncthreads_or(!ok)) {
+        // a bounded wait gave up: let this CTA's MMAs drain (bounded) before
+        // the accumulator is freed, report, leave
+        if (tid == 0) {
+            if (p.err) atomicOr(p.err, 1);
+            for (int s = 0; s < TG_STAGES && nk > 0; ++s) {
+                const int last = (nk - 1 - s);
+                if (last >= 0)
+                    mbar_wait_polls(&mma_bar[last % TG_STAGES],
+                                    (uint32_t)((last / TG_STAGES) & 1), 1 << 16);
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) {
+            tc_fence_after();
+            tmem_dealloc(tmem, BN);
+        }
+        return;
+    }
+    tc_fence_after();
+
+    // epilogue: warp w holds rows 32w..32w+31 (TMEM lanes), 32 columns at a time
+    const int64_t m = m0 + warp * 32 + lane;
+    const bool mok = m < p.M && nk > 0;
+    if (p.tma_c) {
+        // each warp stages its 32 x 32 boxes in two 4 KB buffers (in the first
+        // stage's operand space, free once every MMA is done) with the 128-byte
+        // swizzle, and lane 0 stores (or adds) them with TMA; out-of-range rows
+        // and columns are clipped by the copy
+        float* wb = smem + warp * 2 * 1024;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 32) {
+            float v[32];
+            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
+            const int64_t nb = n0 + c;
+            if (nb >= p.N) break;  // uniform across the CTA
+            if (p.E && mok) {
+                const float* er = p.E + m * p.lde;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                    if (nb + j < p.N) v[j] = fmaf(p.evec[nb + j], er[nb + j], v[j]);
+            }
+            float* buf = wb + ((c >> 5) & 1) * 1024;
+            if (lane == 0) bulk_wait_read<1>();  // the box this buffer held last has left
+            __syncwarp();
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+                reinterpret_cast<float4*>(buf + lane * 32)[j ^ (lane & 7)] =
+                    make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {
+                tma_store_2d(&maps.c, buf, (int)nb, (int)(m0 + warp * 32), p.accumulate != 0);
+                bulk_commit();
+            }
+        }
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+    } else {
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
+        const int64_t nb = n0 + c;
+        if (!mok || nb >= p.N) continue;
+        if (p.E) {
+            const float* er = p.E + m * p.lde;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+                if (nb + j < p.N) v[j] = fmaf(p.evec[nb + j], er[nb + j], v[j]);
+        }
+        float* cr = p.C + m * p.ldc + nb;
+        const bool vec = nb + 32 <= p.N && ((reinterpret_cast<uintptr_t>(cr) & 15) == 0);
+        if (p.accumulate) {
+            if (vec) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4) red_add_v4(cr + j, v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+                for (int j = 0; j < 32 && nb + j < p.N; ++j) atomicAdd(cr + j, v[j]);
+            }
+        } else {
+            if (vec) {
+#pragma unroll
+                for (int j = 0; j < 32; j += 4)
+                    *reinterpret_cast<float4*>(cr + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+            } else {
+                for (int j = 0; j < 32 && nb + j < p.N; ++j) cr[j] = v[j];
+            }
+        }
+    }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem, BN);
+    }
+}
+
+template <int BN, bool A_MN, bool B_MN>
+static int tg_launch(const TGParams& p0, const float* A, int64_t lda, const float* B, int64_t ldb,
+                     int splits, cudaStream_t s) {
+    TGParams p = p0;
+    TGMaps maps;
+    // K-major: dims (K, rows) with rows lda apart; MN-major: (rows, K) with K-rows lda apart
+    const bool oka = A_MN ? mmb_encode_tile_map(&maps.a, A, 4, p.M, p.K, 1, lda, lda * p.K, 32,
+                                                TG_BK, MMB_SWZ_128B_ATOM32)
+                          : mmb_encode_tile_map(&maps.a, A, 4, p.K, p.M, 1, lda, lda * p.M, TG_BK,
+                                                TG_BM, TG_BK * 4);
+    const bool okb = B_MN ? mmb_encode_tile_map(&maps.b, B, 4, p.N, p.K, 1, ldb, ldb * p.K, 32,
+                                                TG_BK, MMB_SWZ_128B_ATOM32)
+                          : mmb_encode_tile_map(&maps.b, B, 4, p.K, p.N, 1, ldb, ldb * p.N, TG_BK,
+                                                BN, TG_BK * 4);
+    if (!oka || !okb) return MMB_ERR_ALIGN;
+    // C through TMA boxes when its base and row pitch are 16-byte aligned
+    p.tma_c = (((uintptr_t)p.C & 15) == 0 && (p.ldc & 3) == 0 &&
+               mmb_encode_tile_map(&maps.c, p.C, 4, p.N, p.M, 1, p.ldc, p.ldc * p.M, 32, 32, 128))
+                  ? 1 : 0;
+    static int attr_done[MMB_MAX_DEVICES] = {};
+    const int st = mmb_smem_attr(tc_gemm_kernel<BN, A_MN, B_MN>, TGSmem<BN>::BYTES, attr_done);
+    if (st != MMB_OK) return st;
+    p.err = mmb_device_error_flag();
+    dim3 grid((unsigned)((p.M + TG_BM - 1) / TG_BM), (unsigned)((p.N + BN - 1) / BN),
+              (unsigned)splits);
+    tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TG_NT, TGSmem<BN>::BYTES, s>>>(p, maps);
+    return mmb_launch_status();
+}
+
+template <int BN>
+static int tg_dispatch(bool a_mn, bool b_mn, const TGParams& p, const float* A, int64_t lda,
+                       const float* B, int64_t ldb, int splits, cudaStream_t s) {
+    if (a_mn) return b_mn ? tg_launch<BN, true, true>(p, A, lda, B, ldb, splits, s)
+                          : tg_launch<BN, true, false>(p, A, lda, B, ldb, splits, s);
+    return b_mn ? tg_launch<BN, false, true>(p, A, lda, B, ldb, splits, s)
+                : tg_launch<BN, false, false>(p, A, lda, B, ldb, splits, s);
+}
+
+}  // namespace mmb
+
+using namespace mmb;
+
+extern "C" int mmb_gemm_f32(int32_t a_mn, int32_t b_mn, int64_t M, int64_t N, int64_t K,
+                            const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
+                            int64_t ldc, const float* E, int64_t lde, const float* evec,
+                            int32_t accumulate, int32_t splits, mmb_stream_t stream) {
+    MMB_NVTX("mmb_gemm_f32");
+    if (!A || !B || !C || (E && !evec)) return MMB_ERR_NULL;
+    if (M <= 0 || N <= 0 || K <= 0 || splits < 1 || splits > 65535) return MMB_ERR_SHAPE;
+    if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return MMB_ERR_SHAPE;
+    if (ldc < N || (E && lde < N)) return MMB_ERR_SHAPE;
+    if ((a_mn ? lda < M : lda < K) || (b_mn ? ldb < N : ldb < K)) return MMB_ERR_SHAPE;
+    // TMA: 16-byte aligned bases and row pitches
+    if (((uintptr_t)A & 15) || ((uintptr_t)B & 15) || (lda & 3) || (ldb & 3)) return MMB_ERR_ALIGN;
+    if (splits > 1 && !accumulate) return MMB_ERR_SHAPE;
+    TGParams p{};
+    p.M = M; p.N = N; p.K = K;
+    const int64_t per = (K + splits - 1) / splits;
+    p.kchunk = (per + TG_BK - 1) / TG_BK * TG_BK;
+    const int used = (int)((K + p.kchunk - 1) / p.kchunk);
+    p.C = C; p.ldc = ldc; p.E = E; p.lde = lde; p.evec = evec;
+    p.accumulate = accumulate ? 1 : 0;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    // 256-column tiles when N fills them, else 128
+    if (MMB_TG_BN_MAX > 128 && N > 128)
+        return tg_dispatch<256>(a_mn != 0, b_mn != 0, p, A, lda, B, ldb, used, s);
+    return tg_dispatch<128>(a_mn != 0, b_mn != 0, p, A, lda, B, ldb, used, s);
+}
