@@ -55,13 +55,17 @@ constexpr int MM_CK = 8;    // checkpoint interval = steps per register block
 constexpr unsigned FULL = 0xffffffffu;
 // cp.async pipeline depth in chunks (3 and 4 stages measured no faster: the
 // kernels are issue-latency bound, not load-latency bound)
-constexpr int MM_NS = 2;
+#ifndef MMB_MM_STAGES
+#define MMB_MM_STAGES 2
+#endif
+constexpr int MM_NS = MMB_MM_STAGES;
 
 __host__ __device__ constexpr int ilog2c(int v) { return v <= 1 ? 0 : 1 + ilog2c(v / 2); }
 
-template <int N, int NP, int NT = MM_NT>
+template <int N, int NP, int NT = MM_NT, int TS = MM_T>
 struct MMCfg {
     static constexpr int NTH = NT;                    // threads per CTA
+    static constexpr int T = TS;                      // steps per staged chunk
     static constexpr int NP2 = NP / 2;                // packed pairs per thread
     static constexpr int G = N / NP;                  // lanes per channel
     static constexpr int LOG2G = ilog2c(G);
@@ -74,15 +78,16 @@ struct MMCfg {
     // chunks are XOR-swizzled across rows -- the TMA swizzle of a DT*4-byte row
     // (up to 128 bytes) -- so the rows and channels a warp reads at once fall
     // in distinct banks.  (T x N) tiles of B and C are dense, unswizzled.
-    static constexpr int TR = MM_T * DT;
+    static constexpr int TR = TS * DT;
     static constexpr int SWB = DT * 4 <= 128 ? DT * 4 : 0;  // swizzle span in bytes
     static constexpr int SWM = SWB ? SWB / 4 - 4 : 0;        // its XOR mask in floats
     __host__ __device__ static constexpr int dix(int r, int c) {
         return (r * DT + c) ^ (((r * DT + c) >> 3) & SWM);
     }
-    static constexpr int TN = MM_T * N;
+    static constexpr int TN = TS * N;
     static_assert((NP == 2 || NP == 4) && N % NP == 0 && G >= 2 && G <= 16 && DT >= 4,
                   "unsupported shape");
+    static_assert(TS % MM_CK == 0 && MM_T % TS == 0, "staged chunks hold whole 8-step blocks");
 };
 
 // Shared-memory layout of one kernel: NDT (T x DT) activation tiles and two
@@ -92,12 +97,12 @@ struct MMCfg {
 // kernel widens.  Stages start on 1024-byte boundaries (the swizzle period);
 // MM_SMEM_ALIGN bytes of slack let the kernel align its dynamic base.
 constexpr int MM_SMEM_ALIGN = 1024;
-template <int N, int NP, int NDT, int EBYTES, int NT = MM_NT>
+template <int N, int NP, int NDT, int EBYTES, int NT = MM_NT, int TS = MM_T>
 struct MMSmem {
-    using Cf = MMCfg<N, NP, NT>;
+    using Cf = MMCfg<N, NP, NT, TS>;
     static constexpr bool WIDE = EBYTES == 2;
     static constexpr int F32 = NDT * Cf::TR + 2 * Cf::TN;             // floats per fp32 stage
-    static constexpr int RAW = NDT * MM_T * Cf::DT + 2 * MM_T * N;    // 16-bit words per raw stage
+    static constexpr int RAW = NDT * TS * Cf::DT + 2 * TS * N;        // 16-bit words per raw stage
     static constexpr int FLOATS = WIDE ? F32 + MM_NS * RAW / 2 : MM_NS * F32;
     static_assert((F32 * 4) % MM_SMEM_ALIGN == 0, "stage size keeps the swizzle period");
 };
@@ -240,7 +245,7 @@ struct MMRange {
     int cb, ce;  // staged chunks [cb, ce)
 };
 // TCH false: the whole sequence (a kernel built for calls that do not split).
-template <bool TCH = true>
+template <bool TCH = true, int TS = MM_T>
 __device__ __forceinline__ MMRange mm_range(const MMParams& p, int64_t b, int64_t d) {
     MMRange r;
     if constexpr (TCH) {
@@ -253,8 +258,8 @@ __device__ __forceinline__ MMRange mm_range(const MMParams& p, int64_t b, int64_
         r.te = p.L;
         r.rec = b * p.D + d;
     }
-    r.cb = (int)(r.tb / MM_T);
-    r.ce = (int)((r.te + MM_T - 1) / MM_T);
+    r.cb = (int)(r.tb / TS);
+    r.ce = (int)((r.te + TS - 1) / TS);
     return r;
 }
 
@@ -293,10 +298,10 @@ __device__ __forceinline__ void ckpt_load(const float* src, float2 (&h)[NP / 2],
 // the tiles it is about to copy and issues one tensor copy per tile; the other
 // threads only wait on the barrier.  Otherwise every thread issues cp.async
 // copies and waits on its own groups.
-template <int N, int NP, int NDT, class E, int NT = MM_NT>
+template <int N, int NP, int NDT, class E, int NT = MM_NT, int TS = MM_T>
 struct MMStager {
-    using Cf = MMCfg<N, NP, NT>;
-    using Sm = MMSmem<N, NP, NDT, E::BYTES, NT>;
+    using Cf = MMCfg<N, NP, NT, TS>;
+    using Sm = MMSmem<N, NP, NDT, E::BYTES, NT, TS>;
     using ET = typename E::T;
     float* smem;      // aligned dynamic base
     uint64_t* bars;   // MM_NS transaction barriers
@@ -307,11 +312,11 @@ struct MMStager {
         return reinterpret_cast<uint16_t*>(smem + Sm::F32) + slot * Sm::RAW;
     }
     __device__ void* dtile(int slot, int i) const {
-        if constexpr (Sm::WIDE) return raw(slot) + i * MM_T * Cf::DT;
+        if constexpr (Sm::WIDE) return raw(slot) + i * TS * Cf::DT;
         else return smem + slot * Sm::F32 + i * Cf::TR;
     }
     __device__ void* ntile(int slot, int j) const {
-        if constexpr (Sm::WIDE) return raw(slot) + NDT * MM_T * Cf::DT + j * MM_T * N;
+        if constexpr (Sm::WIDE) return raw(slot) + NDT * TS * Cf::DT + j * TS * N;
         else return smem + slot * Sm::F32 + NDT * Cf::TR + j * Cf::TN;
     }
     // open a stage that will hold nd activation tiles and nn B/C tiles
@@ -326,11 +331,11 @@ struct MMStager {
             return;
         }
         if constexpr (Sm::WIDE)
-            stage_tile_b16<MM_T, Cf::DT, Cf::DT, NT>(static_cast<uint16_t*>(dtile(slot, i)),
+            stage_tile_b16<TS, Cf::DT, Cf::DT, NT>(static_cast<uint16_t*>(dtile(slot, i)),
                                                         reinterpret_cast<const uint16_t*>(g),
                                                         gstride, rows, dcols, tid);
         else
-            stage_tile_swz<MM_T, Cf::DT, Cf::SWM, NT>(static_cast<float*>(dtile(slot, i)),
+            stage_tile_swz<TS, Cf::DT, Cf::SWM, NT>(static_cast<float*>(dtile(slot, i)),
                                                          reinterpret_cast<const float*>(g),
                                                          gstride, rows, dcols, vec, tid);
     }
@@ -341,11 +346,11 @@ struct MMStager {
             return;
         }
         if constexpr (Sm::WIDE)
-            stage_tile_b16<MM_T, N, N, NT>(static_cast<uint16_t*>(ntile(slot, j)),
+            stage_tile_b16<TS, N, N, NT>(static_cast<uint16_t*>(ntile(slot, j)),
                                               reinterpret_cast<const uint16_t*>(g), gstride, rows,
                                               N, tid);
         else
-            stage_tile_swz<MM_T, N, 0, NT>(static_cast<float*>(ntile(slot, j)),
+            stage_tile_swz<TS, N, 0, NT>(static_cast<float*>(ntile(slot, j)),
                                               reinterpret_cast<const float*>(g), gstride, rows,
                                               N, vec, tid);
     }
@@ -367,13 +372,13 @@ struct MMStager {
 #pragma unroll
             for (int i = 0; i < NDT; ++i)
                 if (dmask & (1u << i))
-                    widen_tile_swz<MM_T, Cf::DT, Cf::SWM, NT>(smem + i * Cf::TR,
-                                                                 r + i * MM_T * Cf::DT, tid);
+                    widen_tile_swz<TS, Cf::DT, Cf::SWM, NT>(smem + i * Cf::TR,
+                                                               r + i * TS * Cf::DT, tid);
 #pragma unroll
             for (int j = 0; j < 2; ++j)
                 if (nmask & (1u << j))
-                    widen_tile_swz<MM_T, N, 0, NT>(smem + NDT * Cf::TR + j * Cf::TN,
-                                                      r + NDT * MM_T * Cf::DT + j * MM_T * N, tid);
+                    widen_tile_swz<TS, N, 0, NT>(smem + NDT * Cf::TR + j * Cf::TN,
+                                                    r + NDT * TS * Cf::DT + j * TS * N, tid);
             return smem;
         } else {
             return smem + slot * Sm::F32;
@@ -671,28 +676,40 @@ __host__ __device__ constexpr bool mm_bwd_cbuf() { return N <= 32 && NT > 32; }
 // stores hit distinct banks); after the window each warp sums its own DPW
 // channels' rows and adds the results to global memory with vector reductions.
 // ---------------------------------------------------------------------------
-// (min 1 block per SM: without it ptxas caps the registers for 3 blocks per SM
-// and spills; the 254-register build measured 7-8 % faster)
-template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, int NT>
-__global__ void __launch_bounds__(NT, 1)
+// Minimum resident one-warp CTAs per SM the backward is compiled for (its
+// register cap: 12 -> 168 registers, no spills).  128-thread CTAs keep one as
+// their minimum: with three, ptxas capped them at 168 registers and spilled.
+#ifndef MMB_BWD_MIN_WARPS
+#define MMB_BWD_MIN_WARPS 1
+#endif
+// Steps of dB | dC terms the window buffer holds before its d-sum (8: once per
+// window; 4: twice per window, half the buffer).
+#ifndef MMB_BWD_WBUF_STEPS
+#define MMB_BWD_WBUF_STEPS 8
+#endif
+constexpr int MM_BWD_WBUF_STEPS = MMB_BWD_WBUF_STEPS;
+template <int N, int NP, bool SOFTPLUS, bool HAS_Z, class E, int NT, int TS>
+__global__ void __launch_bounds__(NT, (NT == 32 ? MMB_BWD_MIN_WARPS : 1))
     mmscan_bwd_kernel(const MMParams p, const __grid_constant__ MMTmaps tmaps) {
-    using Cf = MMCfg<N, NP, NT>;
-    using Sm = MMSmem<N, NP, 4, E::BYTES, NT>;
+    using Cf = MMCfg<N, NP, NT, TS>;
+    using Sm = MMSmem<N, NP, 4, E::BYTES, NT, TS>;
     using ET = typename E::T;
-    constexpr int DT = Cf::DT, G = Cf::G, T = MM_T, IPL = Cf::IPL, LB = Cf::LB;
+    constexpr int DT = Cf::DT, G = Cf::G, T = TS, IPL = Cf::IPL, LB = Cf::LB;
     constexpr int NP2 = Cf::NP2, TR = Cf::TR, DPW = Cf::DPW;
     constexpr int NQ = 2 * N / 4;  // float4 columns per window-buffer row
     constexpr int SWZ = NQ / 2;    // float4 swizzle of odd channels (= G units of NP floats)
+    constexpr int WB = MM_BWD_WBUF_STEPS;  // steps the window buffer holds
     extern __shared__ float4 smem4[];
     __shared__ uint64_t bars[MM_NS];
     // tiles: x | delta | z | dout (T x DT), B | C (T x N); then the window buffer
-    MMStager<N, NP, 4, E, NT> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0, p.vec, p.tma};
+    MMStager<N, NP, 4, E, NT, TS> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0,
+                                      p.vec, p.tma};
     mm_pipe_init(bars, p.tma);
     float* wbuf = stg.smem + Sm::FLOATS;
     // chunk buffer (N <= 32): each warp's d-sums of dB | dC for the 32 steps of
     // a chunk, [warp][step][2N]; summed over the CTA's warps once per chunk
     constexpr bool CBUF = mm_bwd_cbuf<N, NT>();
-    float4* cbuf = reinterpret_cast<float4*>(wbuf + MM_CK * DT * 2 * N);
+    float4* cbuf = reinterpret_cast<float4*>(wbuf + WB * DT * 2 * N);
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int ng = lane & (G - 1);
@@ -705,7 +722,7 @@ __global__ void __launch_bounds__(NT, 1)
     const int64_t d = d0 + dl;
     const bool dvalid = d < p.D;
     stg.dcols = (int)min64(DT, p.D - d0);
-    const MMRange rg = mm_range(p, b, d);
+    const MMRange rg = mm_range<true, TS>(p, b, d);
     const int64_t te = rg.te;
     const int swz_units = (dl & 1) ? G : 0;
     const ET* gx = static_cast<const ET*>(p.x);
@@ -799,6 +816,50 @@ __global__ void __launch_bounds__(NT, 1)
 
         for (int w = (Lc - 1) / MM_CK; w >= 0; --w) {
             const int w0 = w * MM_CK;
+            // d-sum of this warp's rows of the window buffer (its DPW channels)
+            // for the WB steps from s0: one vector reduction per (step, 4
+            // columns), or into the chunk buffer
+            auto wsum = [&](int s0) {
+                constexpr int ITEMS = WB * NQ;
+                constexpr int IPT = ITEMS >= 32 ? ITEMS / 32 : 1;
+                constexpr int TPI = ITEMS >= 32 ? 1 : 32 / ITEMS;
+                constexpr int RPT = DPW / TPI > 0 ? DPW / TPI : 1;
+#pragma unroll
+                for (int j = 0; j < IPT; ++j) {
+                    const int item = (lane / TPI) + j * (32 / TPI), part = lane % TPI;
+                    const int sb = item / NQ, q = item % NQ;  // buffer row group, column
+                    const int s = s0 + sb;
+                    float2 acc01 = f2(0.f), acc23 = f2(0.f);
+#pragma unroll
+                    for (int r = 0; r < RPT; ++r) {
+                        const int row = warp * DPW + part * RPT + r;
+                        const float4 vv = reinterpret_cast<const float4*>(
+                            wbuf + (sb * DT + row) * 2 * N)[q ^ ((row & 1) ? SWZ : 0)];
+                        acc01 = fadd2(acc01, make_float2(vv.x, vv.y));
+                        acc23 = fadd2(acc23, make_float2(vv.z, vv.w));
+                    }
+#pragma unroll
+                    for (int m = 1; m < TPI; m <<= 1) {
+                        acc01.x += __shfl_xor_sync(FULL, acc01.x, m);
+                        acc01.y += __shfl_xor_sync(FULL, acc01.y, m);
+                        acc23.x += __shfl_xor_sync(FULL, acc23.x, m);
+                        acc23.y += __shfl_xor_sync(FULL, acc23.y, m);
+                    }
+                    if constexpr (CBUF) {
+                        if (part == 0)
+                            cbuf[(warp * T + w0 + s) * NQ + q] =
+                                make_float4(acc01.x, acc01.y, acc23.x, acc23.y);
+                    } else {
+                        const int64_t gt = t0 + w0 + s;
+                        if (part == 0 && gt < te) {
+                            const int col = q * 4;
+                            float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
+                            red_add_v4(dst, acc01.x, acc01.y, acc23.x, acc23.y);
+                        }
+                    }
+                }
+                __syncwarp();
+            };
             // window checkpoint (loaded one window ahead)
             if (it == 0 && w == (Lc - 1) / MM_CK) ck_next();
             float2 h[NP2], v[NP2];
@@ -896,7 +957,7 @@ __global__ void __launch_bounds__(NT, 1)
                 sab[2 * s] = sa.x + sa.y;
                 sab[2 * s + 1] = sb.x + sb.y;
                 // dB | dC terms of (t, d, this lane's states) into the window buffer
-                float* rowp = wrow + s * DT * 2 * N;
+                float* rowp = wrow + (s % WB) * DT * 2 * N;
                 if constexpr (NP == 4) {
                     float4* r4 = reinterpret_cast<float4*>(rowp);
                     r4[ng ^ swz_units] = make_float4(pb[0].x, pb[0].y, pb[1].x, pb[1].y);
@@ -905,6 +966,10 @@ __global__ void __launch_bounds__(NT, 1)
                     float2* r2 = reinterpret_cast<float2*>(rowp);
                     r2[ng ^ swz_units] = pb[0];
                     r2[(G + ng) ^ swz_units] = pc[0];
+                }
+                if (WB < MM_CK && s % WB == 0) {  // a group of WB steps is complete
+                    __syncwarp();
+                    wsum(s);
                 }
             }
             // n-sums back to the owning lanes: sab[2i], sab[2i + 1] = (SA, SB) of item i
@@ -934,47 +999,7 @@ __global__ void __launch_bounds__(NT, 1)
                 }
             }
             __syncwarp();
-            // d-sum of this warp's rows of the window buffer (its DPW channels)
-            {
-                constexpr int ITEMS = MM_CK * NQ;
-                constexpr int IPT = ITEMS >= 32 ? ITEMS / 32 : 1;
-                constexpr int TPI = ITEMS >= 32 ? 1 : 32 / ITEMS;
-                constexpr int RPT = DPW / TPI > 0 ? DPW / TPI : 1;
-#pragma unroll
-                for (int j = 0; j < IPT; ++j) {
-                    const int item = (lane / TPI) + j * (32 / TPI), part = lane % TPI;
-                    const int s = item / NQ, q = item % NQ;
-                    float2 acc01 = f2(0.f), acc23 = f2(0.f);
-#pragma unroll
-                    for (int r = 0; r < RPT; ++r) {
-                        const int row = warp * DPW + part * RPT + r;
-                        const float4 vv = reinterpret_cast<const float4*>(
-                            wbuf + (s * DT + row) * 2 * N)[q ^ ((row & 1) ? SWZ : 0)];
-                        acc01 = fadd2(acc01, make_float2(vv.x, vv.y));
-                        acc23 = fadd2(acc23, make_float2(vv.z, vv.w));
-                    }
-#pragma unroll
-                    for (int m = 1; m < TPI; m <<= 1) {
-                        acc01.x += __shfl_xor_sync(FULL, acc01.x, m);
-                        acc01.y += __shfl_xor_sync(FULL, acc01.y, m);
-                        acc23.x += __shfl_xor_sync(FULL, acc23.x, m);
-                        acc23.y += __shfl_xor_sync(FULL, acc23.y, m);
-                    }
-                    if constexpr (CBUF) {
-                        if (part == 0)
-                            cbuf[(warp * T + w0 + s) * NQ + q] =
-                                make_float4(acc01.x, acc01.y, acc23.x, acc23.y);
-                    } else {
-                        const int64_t gt = t0 + w0 + s;
-                        if (part == 0 && gt < te) {
-                            const int col = q * 4;
-                            float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
-                            red_add_v4(dst, acc01.x, acc01.y, acc23.x, acc23.y);
-                        }
-                    }
-                }
-            }
-            __syncwarp();
+            if constexpr (WB == MM_CK) wsum(0);
         }
         __syncthreads();
         if constexpr (CBUF) {
@@ -1193,9 +1218,9 @@ __global__ void __launch_bounds__(MM_NT)
 // Tensor maps of the activation and B/C tiles a launch stages; false (and the
 // kernel falls back to cp.async) when the rows are not 16-byte aligned or the
 // driver declines an encoding.
-template <int N, int NP, class E, int NT = MM_NT>
+template <int N, int NP, class E, int NT = MM_NT, int TS = MM_T>
 bool mm_build_tmaps(const MMParams& p, MMTmaps& tm) {
-    using Cf = MMCfg<N, NP, NT>;
+    using Cf = MMCfg<N, NP, NT, TS>;
     if (!p.vec) return false;
     const int eb = E::BYTES;
     const int swz = eb == 4 ? Cf::SWB : 0;  // bf16 raw tiles land unswizzled
@@ -1207,22 +1232,22 @@ bool mm_build_tmaps(const MMParams& p, MMTmaps& tm) {
     for (const Act& a : acts) {
         if (!a.ptr) continue;
         if (!mmb_encode_tile_map(&tm.m[a.slot], a.ptr, eb, p.D, p.L, p.Bsz, a.s1, a.s0, Cf::DT,
-                                 MM_T, swz))
+                                 TS, swz))
             return false;
     }
     const Act bc[2] = {{TM_B, p.Bm, p.bs[1], p.bs[0]}, {TM_C, p.Cm, p.cs[1], p.cs[0]}};
     for (const Act& a : bc) {
         if (!a.ptr) continue;
-        if (!mmb_encode_tile_map(&tm.m[a.slot], a.ptr, eb, N, p.L, p.Bsz, a.s1, a.s0, N, MM_T, 0))
+        if (!mmb_encode_tile_map(&tm.m[a.slot], a.ptr, eb, N, p.L, p.Bsz, a.s1, a.s0, N, TS, 0))
             return false;
     }
     return true;
 }
 
-template <int N, int NP, class E, int NT = MM_NT>
+template <int N, int NP, class E, int NT = MM_NT, int TS = MM_T>
 MMParams mm_launch_params(const MMParams& p0, MMTmaps& tm) {
     MMParams p = p0;
-    p.tma = mm_build_tmaps<N, NP, E, NT>(p, tm) ? 1 : 0;
+    p.tma = mm_build_tmaps<N, NP, E, NT, TS>(p, tm) ? 1 : 0;
     p.err = mmb_device_error_flag();
     return p;
 }
@@ -1276,22 +1301,28 @@ int launch_fwd_t(const MMParams& p0, cudaStream_t stream) {
     return launch_fwd_nt<N, NP, SP, Z, E, SUMM, MM_NT>(p0, stream);
 }
 
+#ifndef MMB_BWD_T
+#define MMB_BWD_T MM_T
+#endif
 template <int N, int NP, bool SP, bool Z, class E>
 int launch_bwd_t(const MMParams& p0, cudaStream_t stream) {
     // 32 threads only where a CTA keeps at least 8 channels (32-byte tile rows)
     constexpr int NT = (MMB_BWD_NT == 32 && 32 / (N / NP) >= 8) ? 32 : MM_NT;
-    using Cf = MMCfg<N, NP, NT>;
+    // steps per staged chunk: one-warp CTAs stage MMB_BWD_T
+    constexpr int TS = NT == 32 ? MMB_BWD_T : MM_T;
+    using Cf = MMCfg<N, NP, NT, TS>;
     const size_t smem =
-        sizeof(float) * (MMSmem<N, NP, 4, E::BYTES, NT>::FLOATS + MM_CK * Cf::DT * 2 * N +
-                         (mm_bwd_cbuf<N, NT>() ? (NT / 32) * MM_T * 2 * N : 0)) +
+        sizeof(float) * (MMSmem<N, NP, 4, E::BYTES, NT, TS>::FLOATS +
+                         MM_BWD_WBUF_STEPS * Cf::DT * 2 * N +
+                         (mm_bwd_cbuf<N, NT>() ? (NT / 32) * TS * 2 * N : 0)) +
         MM_SMEM_ALIGN;
     static int attr_done[MMB_MAX_DEVICES] = {};
-    const int st = mmb_smem_attr(mmscan_bwd_kernel<N, NP, SP, Z, E, NT>, smem, attr_done);
+    const int st = mmb_smem_attr(mmscan_bwd_kernel<N, NP, SP, Z, E, NT, TS>, smem, attr_done);
     if (st != MMB_OK) return st;
     MMTmaps tm;
-    const MMParams p = mm_launch_params<N, NP, E, NT>(p0, tm);
+    const MMParams p = mm_launch_params<N, NP, E, NT, TS>(p0, tm);
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz, (unsigned)p.nz);
-    mmscan_bwd_kernel<N, NP, SP, Z, E, NT><<<grid, NT, smem, stream>>>(p, tm);
+    mmscan_bwd_kernel<N, NP, SP, Z, E, NT, TS><<<grid, NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }
 
