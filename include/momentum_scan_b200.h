@@ -402,15 +402,28 @@ int mmb_scan2_fwd_noalloc(int64_t batch, int64_t L, int64_t P, int32_t complex_f
  * C and E row-major with ldc, lde >= N.  A, B 16-byte aligned, lda and ldb
  * multiples of 4.  Each operand is split into a tf32 high part and an fp32
  * remainder; the three significant partial products are accumulated in fp32
- * (error within a few fp32 ulps of the products).  accumulate != 0 adds into
- * C with vector reductions (C cleared by the caller); splits > 1 cuts K into
- * that many slices, one CTA per slice and tile (needs accumulate).  E, evec
- * nullable (both or neither).
+ * (error within a few fp32 ulps of the products).  B_lo nullable: when given,
+ * B holds the high parts and B_lo the remainders of a K-major B (as
+ * mmb_split_tf32 makes them, e.g. once per call for weights), and only A is
+ * split per tile.  accumulate != 0 adds into C with vector reductions (C
+ * cleared by the caller); splits > 1 cuts K into that many slices, one CTA
+ * per slice and tile (needs accumulate).  E, evec nullable (both or neither).
  * ========================================================================= */
 int mmb_gemm_f32(int32_t a_mn, int32_t b_mn, int64_t M, int64_t N, int64_t K, const float* A,
-                 int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
-                 const float* E, int64_t lde, const float* evec, int32_t accumulate,
-                 int32_t splits, mmb_stream_t stream);
+                 int64_t lda, const float* B, const float* B_lo, int64_t ldb, float* C,
+                 int64_t ldc, const float* E, int64_t lde, const float* evec,
+                 int32_t accumulate, int32_t splits, mmb_stream_t stream);
+
+/* hi = x with the low 13 mantissa bits cleared (exact in tf32), lo = x - hi,
+ * n floats each. */
+int mmb_split_tf32(const float* x, float* hi, float* lo, int64_t n, mmb_stream_t stream);
+
+/* out[n] (= or +=) sum_m X[m * ldx + n] * Y[m * ldy + n] for n < N: the
+ * feedthrough gradient d(D) = sum over (b, t) of dy * u of the LinOSS layer
+ * (LinOSS_pytorch.py:306-312).  N, ldx, ldy multiples of 4, X and Y 16-byte
+ * aligned. */
+int mmb_col_dot_f32(int64_t M, int64_t N, const float* X, int64_t ldx, const float* Y,
+                    int64_t ldy, float* out, int32_t accumulate, mmb_stream_t stream);
 
 /* =========================================================================
  * LinOSS layer scan with a time-invariant transition per oscillator p -- the

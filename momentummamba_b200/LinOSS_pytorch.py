@@ -22,7 +22,7 @@ import torch.nn.functional as F
 
 from . import _lib
 from .scan2 import _DISC, _real_view, linoss_scan, scan2
-from .tc_gemm import gemm_nt, gemm_tn
+from .tc_gemm import col_dot, gemm_nt, gemm_tn, split_tf32
 
 VMAP_AVAILABLE = True
 
@@ -98,7 +98,7 @@ class LinOSSLayerFn(torch.autograd.Function):
         u2 = u.reshape(Bsz * L, H).float().contiguous()
         Bm = torch.stack([B_real.float(), B_imag.float()], dim=1).reshape(2 * P, H)
         Cc = torch.stack([C_real.float(), -C_imag.float()], dim=2).reshape(H, 2 * P)
-        Bu = gemm_nt(u2, Bm).view(Bsz, L, P, 2)
+        Bu = gemm_nt(u2, split_tf32(Bm)).view(Bsz, L, P, 2)
         A, s = A_diag.float().contiguous(), step.float().contiguous()
         lib = _lib.load()
         x2 = torch.empty_like(Bu)
@@ -109,7 +109,8 @@ class LinOSSLayerFn(torch.autograd.Function):
                                     _lib.stream_of(u))
         _lib.check(st, "mmb_linoss_fwd")
         Dv = D.float().contiguous() if D is not None else None
-        y = gemm_nt(x2.view(Bsz * L, 2 * P), Cc, E=u2 if Dv is not None else None, evec=Dv)
+        y = gemm_nt(x2.view(Bsz * L, 2 * P), split_tf32(Cc), E=u2 if Dv is not None else None,
+                    evec=Dv)
         ctx.save_for_backward(A, s, Bm, Cc, u2, Bu, x2, work, Dv)
         ctx.disc, ctx.has_d, ctx.shape = disc, Dv is not None, (Bsz, L, H, P)
         return y.view(Bsz, L, H)
@@ -119,7 +120,7 @@ class LinOSSLayerFn(torch.autograd.Function):
         A, s, Bm, Cc, u2, Bu, x2, work, Dv = ctx.saved_tensors
         Bsz, L, H, P = ctx.shape
         dy2 = dy.reshape(Bsz * L, H).float().contiguous()
-        dx2 = gemm_nt(dy2, Cc.t().contiguous())                    # (B L, 2P)
+        dx2 = gemm_nt(dy2, split_tf32(Cc.t()))                     # (B L, 2P)
         lib = _lib.load()
         dBu = torch.empty_like(Bu)
         dA = torch.empty_like(A)
@@ -130,11 +131,11 @@ class LinOSSLayerFn(torch.autograd.Function):
                                     _lib.ptr(ds), _lib.ptr(work), _lib.stream_of(A))
         _lib.check(st, "mmb_linoss_bwd")
         dBu2 = dBu.view(Bsz * L, 2 * P)
-        du = gemm_nt(dBu2, Bm.t().contiguous(), E=dy2 if ctx.has_d else None,
+        du = gemm_nt(dBu2, split_tf32(Bm.t()), E=dy2 if ctx.has_d else None,
                      evec=Dv if ctx.has_d else None)
         dBm = gemm_tn(dBu2, u2)                                     # (2P, H)
         dCc = gemm_tn(dy2, x2.view(Bsz * L, 2 * P))                 # (H, 2P)
-        dD = (dy2 * u2).sum(0) if ctx.has_d else None
+        dD = (col_dot(dy2, u2) if H % 4 == 0 else (dy2 * u2).sum(0)) if ctx.has_d else None
         dBm = dBm.view(P, 2, H)
         dCc = dCc.view(H, P, 2)
         return (None, dA, ds, dBm[:, 0], dBm[:, 1], dCc[..., 0], -dCc[..., 1], dD,

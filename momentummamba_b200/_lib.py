@@ -99,8 +99,11 @@ _SIGNATURES = {
     "mmb_scan2_fwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i32] + [_c_p] * 6),
     "mmb_scan2_bwd": (ctypes.c_int, [_c_i64, _c_i64, _c_i64, _c_i32] + [_c_p] * 9),
     "mmb_gemm_f32": (ctypes.c_int, [_c_i32, _c_i32, _c_i64, _c_i64, _c_i64, _c_p, _c_i64, _c_p,
-                                    _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i32, _c_i32,
-                                    _c_p]),
+                                    _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i32,
+                                    _c_i32, _c_p]),
+    "mmb_split_tf32": (ctypes.c_int, [_c_p, _c_p, _c_p, _c_i64, _c_p]),
+    "mmb_col_dot_f32": (ctypes.c_int, [_c_i64, _c_i64, _c_p, _c_i64, _c_p, _c_i64, _c_p, _c_i32,
+                                       _c_p]),
     "mmb_linoss_work_floats": (_c_size, [_c_i64, _c_i64, _c_i64]),
     "mmb_linoss_fwd": (ctypes.c_int, [_c_i32, _c_i64, _c_i64, _c_i64] + [_c_p] * 6),
     "mmb_linoss_bwd": (ctypes.c_int, [_c_i32, _c_i64, _c_i64, _c_i64] + [_c_p] * 9),

@@ -134,6 +134,7 @@ struct TGParams {
 };
 struct TGMaps {
     CUtensorMap a, b, c;  // c: 32 x 32 boxes of C, 128-byte swizzle (when p.tma_c)
+    CUtensorMap blo;      // B's low parts when the caller split B (BLO)
 };
 
 // TMA store / reduce-add of one 32 x 32 box of C from shared memory (bulk group)
@@ -210,7 +211,9 @@ __device__ __forceinline__ void tg_split(float* hi, float* lo, int tid) {
     }
 }
 
-template <int BN, bool A_MN, bool B_MN>
+// BLO: B arrives split (B = its tf32 high parts, maps.blo its remainders), as
+// weights split once per call are: only A is split per tile.
+template <int BN, bool A_MN, bool B_MN, bool BLO>
 __global__ void __launch_bounds__(TG_NT)
     tc_gemm_kernel(const TGParams p, const __grid_constant__ TGMaps maps) {
     using Sm = TGSmem<BN>;
@@ -226,7 +229,7 @@ __global__ void __launch_bounds__(TG_NT)
     const int64_t ke = min64(p.K, kb + p.kchunk);
     const int nk = (int)((ke - kb + TG_BK - 1) / TG_BK);
     constexpr uint32_t IDESC = tf32_idesc(BN, A_MN, B_MN);
-    constexpr uint32_t TX = (uint32_t)(TG_BM + BN) * TG_BK * 4;
+    constexpr uint32_t TX = (uint32_t)(TG_BM + (BLO ? 2 : 1) * BN) * TG_BK * 4;
 
     if (tid == 0) {
         for (int s = 0; s < TG_STAGES; ++s) {
@@ -251,6 +254,7 @@ __global__ void __launch_bounds__(TG_NT)
         mbar_expect_tx(&tma_bar[s], TX);
         tg_load<TG_BM, A_MN>(a_hi(s), &maps.a, m0, k0, &tma_bar[s]);
         tg_load<BN, B_MN>(b_hi(s), &maps.b, n0, k0, &tma_bar[s]);
+        if constexpr (BLO) tg_load<BN, B_MN>(b_lo(s), &maps.blo, n0, k0, &tma_bar[s]);
     };
 
     bool ok = true;
@@ -267,7 +271,7 @@ __global__ void __launch_bounds__(TG_NT)
         if (ok) ok = mbar_wait_bounded(&tma_bar[s], (uint32_t)((i / TG_STAGES) & 1));
         if (__syncthreads_or(!ok)) break;
         tg_split<Sm::A_FLOATS>(a_hi(s), a_lo(s), tid);
-        tg_split<Sm::B_FLOATS>(b_hi(s), b_lo(s), tid);
+        if constexpr (!BLO) tg_split<Sm::B_FLOATS>(b_hi(s), b_lo(s), tid);
         fence_proxy_async_smem();
         __syncthreads();
         if (tid == 0) {
@@ -390,9 +394,9 @@ __global__ void __launch_bounds__(TG_NT)
     }
 }
 
-template <int BN, bool A_MN, bool B_MN>
-static int tg_launch(const TGParams& p0, const float* A, int64_t lda, const float* B, int64_t ldb,
-                     int splits, cudaStream_t s) {
+template <int BN, bool A_MN, bool B_MN, bool BLO>
+static int tg_launch(const TGParams& p0, const float* A, int64_t lda, const float* B,
+                     const float* Blo, int64_t ldb, int splits, cudaStream_t s) {
     TGParams p = p0;
     TGMaps maps;
     // K-major: dims (K, rows) with rows lda apart; MN-major: (rows, K) with K-rows lda apart
@@ -405,27 +409,84 @@ static int tg_launch(const TGParams& p0, const float* A, int64_t lda, const floa
                           : mmb_encode_tile_map(&maps.b, B, 4, p.K, p.N, 1, ldb, ldb * p.N, TG_BK,
                                                 BN, TG_BK * 4);
     if (!oka || !okb) return MMB_ERR_ALIGN;
+    if (BLO && !mmb_encode_tile_map(&maps.blo, Blo, 4, p.K, p.N, 1, ldb, ldb * p.N, TG_BK, BN,
+                                    TG_BK * 4))
+        return MMB_ERR_ALIGN;
     // C through TMA boxes when its base and row pitch are 16-byte aligned
     p.tma_c = (((uintptr_t)p.C & 15) == 0 && (p.ldc & 3) == 0 &&
                mmb_encode_tile_map(&maps.c, p.C, 4, p.N, p.M, 1, p.ldc, p.ldc * p.M, 32, 32, 128))
                   ? 1 : 0;
     static int attr_done[MMB_MAX_DEVICES] = {};
-    const int st = mmb_smem_attr(tc_gemm_kernel<BN, A_MN, B_MN>, TGSmem<BN>::BYTES, attr_done);
+    const int st =
+        mmb_smem_attr(tc_gemm_kernel<BN, A_MN, B_MN, BLO>, TGSmem<BN>::BYTES, attr_done);
     if (st != MMB_OK) return st;
     p.err = mmb_device_error_flag();
     dim3 grid((unsigned)((p.M + TG_BM - 1) / TG_BM), (unsigned)((p.N + BN - 1) / BN),
               (unsigned)splits);
-    tc_gemm_kernel<BN, A_MN, B_MN><<<grid, TG_NT, TGSmem<BN>::BYTES, s>>>(p, maps);
+    tc_gemm_kernel<BN, A_MN, B_MN, BLO><<<grid, TG_NT, TGSmem<BN>::BYTES, s>>>(p, maps);
     return mmb_launch_status();
 }
 
 template <int BN>
 static int tg_dispatch(bool a_mn, bool b_mn, const TGParams& p, const float* A, int64_t lda,
-                       const float* B, int64_t ldb, int splits, cudaStream_t s) {
-    if (a_mn) return b_mn ? tg_launch<BN, true, true>(p, A, lda, B, ldb, splits, s)
-                          : tg_launch<BN, true, false>(p, A, lda, B, ldb, splits, s);
-    return b_mn ? tg_launch<BN, false, true>(p, A, lda, B, ldb, splits, s)
-                : tg_launch<BN, false, false>(p, A, lda, B, ldb, splits, s);
+                       const float* B, const float* Blo, int64_t ldb, int splits,
+                       cudaStream_t s) {
+    if (Blo) return a_mn ? tg_launch<BN, true, false, true>(p, A, lda, B, Blo, ldb, splits, s)
+                         : tg_launch<BN, false, false, true>(p, A, lda, B, Blo, ldb, splits, s);
+    if (a_mn) return b_mn ? tg_launch<BN, true, true, false>(p, A, lda, B, Blo, ldb, splits, s)
+                          : tg_launch<BN, true, false, false>(p, A, lda, B, Blo, ldb, splits, s);
+    return b_mn ? tg_launch<BN, false, true, false>(p, A, lda, B, Blo, ldb, splits, s)
+                : tg_launch<BN, false, false, false>(p, A, lda, B, Blo, ldb, splits, s);
+}
+
+// out[n] += sum_m X[m, n] Y[m, n]: each thread keeps 4 columns over a stride of
+// rows, the CTA's warps are summed in shared memory, one atomic add per column
+// and CTA (the LinOSS layer's d(D) = sum over (b, t) of dy * u).
+constexpr int CD_NT = 256;
+__global__ void __launch_bounds__(CD_NT)
+    col_dot_kernel(int64_t M, int64_t N, const float* __restrict__ X, int64_t ldx,
+                   const float* __restrict__ Y, int64_t ldy, float* __restrict__ out) {
+    __shared__ float4 part[CD_NT];
+    const int64_t q = (int64_t)blockIdx.y * 32 + (threadIdx.x & 31);  // column quad
+    const int64_t n0 = q * 4;
+    const int rw = threadIdx.x >> 5;                                    // row lane (warp)
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (n0 < N) {
+        for (int64_t m = (int64_t)blockIdx.x * (CD_NT / 32) + rw; m < M;
+             m += (int64_t)gridDim.x * (CD_NT / 32)) {
+            const float4 a = *reinterpret_cast<const float4*>(X + m * ldx + n0);
+            const float4 b = *reinterpret_cast<const float4*>(Y + m * ldy + n0);
+            acc.x = fmaf(a.x, b.x, acc.x);
+            acc.y = fmaf(a.y, b.y, acc.y);
+            acc.z = fmaf(a.z, b.z, acc.z);
+            acc.w = fmaf(a.w, b.w, acc.w);
+        }
+    }
+    part[threadIdx.x] = acc;
+    __syncthreads();
+    if (rw == 0 && n0 < N) {
+        float4 t = acc;
+        for (int w = 1; w < CD_NT / 32; ++w) {
+            const float4 v = part[w * 32 + threadIdx.x];
+            t.x += v.x; t.y += v.y; t.z += v.z; t.w += v.w;
+        }
+        atomicAdd(out + n0, t.x);
+        atomicAdd(out + n0 + 1, t.y);
+        atomicAdd(out + n0 + 2, t.z);
+        atomicAdd(out + n0 + 3, t.w);
+    }
+}
+
+// hi = x with the low 13 mantissa bits cleared, lo = x - hi
+__global__ void split_tf32_kernel(const float* __restrict__ x, float* __restrict__ hi,
+                                  float* __restrict__ lo, int64_t n) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        const float h = __uint_as_float(__float_as_uint(v) & TG_MASK_HI);
+        hi[i] = h;
+        lo[i] = v - h;
+    }
 }
 
 }  // namespace mmb
@@ -433,11 +494,14 @@ static int tg_dispatch(bool a_mn, bool b_mn, const TGParams& p, const float* A, 
 using namespace mmb;
 
 extern "C" int mmb_gemm_f32(int32_t a_mn, int32_t b_mn, int64_t M, int64_t N, int64_t K,
-                            const float* A, int64_t lda, const float* B, int64_t ldb, float* C,
-                            int64_t ldc, const float* E, int64_t lde, const float* evec,
-                            int32_t accumulate, int32_t splits, mmb_stream_t stream) {
+                            const float* A, int64_t lda, const float* B, const float* B_lo,
+                            int64_t ldb, float* C, int64_t ldc, const float* E, int64_t lde,
+                            const float* evec, int32_t accumulate, int32_t splits,
+                            mmb_stream_t stream) {
     MMB_NVTX("mmb_gemm_f32");
     if (!A || !B || !C || (E && !evec)) return MMB_ERR_NULL;
+    if (B_lo && (b_mn || ((uintptr_t)B_lo & 15))) return B_lo && b_mn ? MMB_ERR_UNSUPPORTED
+                                                                      : MMB_ERR_ALIGN;
     if (M <= 0 || N <= 0 || K <= 0 || splits < 1 || splits > 65535) return MMB_ERR_SHAPE;
     if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return MMB_ERR_SHAPE;
     if (ldc < N || (E && lde < N)) return MMB_ERR_SHAPE;
@@ -455,6 +519,36 @@ extern "C" int mmb_gemm_f32(int32_t a_mn, int32_t b_mn, int64_t M, int64_t N, in
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
     // 256-column tiles when N fills them, else 128
     if (MMB_TG_BN_MAX > 128 && N > 128)
-        return tg_dispatch<256>(a_mn != 0, b_mn != 0, p, A, lda, B, ldb, used, s);
-    return tg_dispatch<128>(a_mn != 0, b_mn != 0, p, A, lda, B, ldb, used, s);
+        return tg_dispatch<256>(a_mn != 0, b_mn != 0, p, A, lda, B, B_lo, ldb, used, s);
+    return tg_dispatch<128>(a_mn != 0, b_mn != 0, p, A, lda, B, B_lo, ldb, used, s);
+}
+
+extern "C" int mmb_col_dot_f32(int64_t M, int64_t N, const float* X, int64_t ldx,
+                               const float* Y, int64_t ldy, float* out, int32_t accumulate,
+                               mmb_stream_t stream) {
+    MMB_NVTX("mmb_col_dot_f32");
+    if (!X || !Y || !out) return MMB_ERR_NULL;
+    if (M <= 0 || N <= 0 || ldx < N || ldy < N) return MMB_ERR_SHAPE;
+    if ((N & 3) || (ldx & 3) || (ldy & 3) || ((uintptr_t)X & 15) || ((uintptr_t)Y & 15))
+        return MMB_ERR_ALIGN;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (!accumulate && cudaMemsetAsync(out, 0, (size_t)N * sizeof(float), s) != cudaSuccess)
+        return mmb_launch_status();
+    const int64_t quads = (N / 4 + 31) / 32;
+    const int64_t rows = (M + CD_NT / 32 - 1) / (CD_NT / 32);
+    const int64_t bx = rows < 148 * 8 / quads ? rows : (148 * 8 + quads - 1) / quads;
+    col_dot_kernel<<<dim3((unsigned)(bx > 0 ? bx : 1), (unsigned)quads), CD_NT, 0, s>>>(
+        M, N, X, ldx, Y, ldy, out);
+    return mmb_launch_status();
+}
+
+extern "C" int mmb_split_tf32(const float* x, float* hi, float* lo, int64_t n,
+                              mmb_stream_t stream) {
+    MMB_NVTX("mmb_split_tf32");
+    if (!x || !hi || !lo) return MMB_ERR_NULL;
+    if (n <= 0) return MMB_ERR_SHAPE;
+    const int64_t blocks = (n + 255) / 256;
+    split_tf32_kernel<<<(unsigned)(blocks < 148 * 8 ? blocks : 148 * 8), 256, 0,
+                        reinterpret_cast<cudaStream_t>(stream)>>>(x, hi, lo, n);
+    return mmb_launch_status();
 }

@@ -16,12 +16,14 @@ TOL = 1e-5
 DEV = "cuda:0"
 
 
-def gemm(A, B, M, N, K, a_mn, b_mn, C=None, E=None, evec=None, accumulate=0, splits=1):
+def gemm(A, B, M, N, K, a_mn, b_mn, C=None, E=None, evec=None, accumulate=0, splits=1,
+         B_lo=None):
     lib = _lib.load()
     if C is None:
         C = torch.zeros(M, N, device=DEV)
     P = _lib.ptr
-    st = lib.mmb_gemm_f32(int(a_mn), int(b_mn), M, N, K, P(A), A.stride(0), P(B), B.stride(0),
+    st = lib.mmb_gemm_f32(int(a_mn), int(b_mn), M, N, K, P(A), A.stride(0), P(B),
+                          P(B_lo) if B_lo is not None else None, B.stride(0),
                           P(C), C.stride(0), P(E) if E is not None else None,
                           E.stride(0) if E is not None else 0, P(evec) if evec is not None else None,
                           accumulate, splits, _lib.stream_of(A))
@@ -112,8 +114,39 @@ def test_rejects_bad_arguments():
     A = torch.zeros(8, 8, device=DEV)
     P = _lib.ptr
     s = _lib.stream_of(A)
-    assert lib.mmb_gemm_f32(0, 0, 8, 8, 8, None, 8, P(A), 8, P(A), 8, None, 0, None, 0, 1, s) == 1
-    assert lib.mmb_gemm_f32(0, 0, 0, 8, 8, P(A), 8, P(A), 8, P(A), 8, None, 0, None, 0, 1, s) == 2
-    assert lib.mmb_gemm_f32(0, 0, 8, 8, 8, P(A), 6, P(A), 8, P(A), 8, None, 0, None, 0, 1, s) == 2
+    assert lib.mmb_gemm_f32(0, 0, 8, 8, 8, None, 8, P(A), None, 8, P(A), 8, None, 0, None, 0, 1, s) == 1
+    assert lib.mmb_gemm_f32(0, 0, 0, 8, 8, P(A), 8, P(A), None, 8, P(A), 8, None, 0, None, 0, 1, s) == 2
+    assert lib.mmb_gemm_f32(0, 0, 8, 8, 8, P(A), 6, P(A), None, 8, P(A), 8, None, 0, None, 0, 1, s) == 2
     # split-K must accumulate
-    assert lib.mmb_gemm_f32(0, 0, 8, 8, 8, P(A), 8, P(A), 8, P(A), 8, None, 0, None, 0, 2, s) == 2
+    assert lib.mmb_gemm_f32(0, 0, 8, 8, 8, P(A), 8, P(A), None, 8, P(A), 8, None, 0, None, 0, 2, s) == 2
+    # pre-split B must be K-major
+    assert lib.mmb_gemm_f32(0, 1, 8, 8, 8, P(A), 8, P(A), P(A), 8, P(A), 8, None, 0, None, 0, 1, s) == 4
+
+
+@pytest.mark.parametrize("a_mn", [0, 1])
+def test_presplit_b_matches_float64(a_mn):
+    """B given as (hi, lo) from mmb_split_tf32: only A is split per tile."""
+    M, N, K = 1000, 512, 128
+    g = torch.Generator(device=DEV).manual_seed(21)
+    Af = torch.randn(M, K, device=DEV, generator=g)
+    Bf = torch.randn(N, K, device=DEV, generator=g)
+    A = Af.t().contiguous() if a_mn else Af
+    hi, lo = torch.empty_like(Bf), torch.empty_like(Bf)
+    lib = _lib.load()
+    _lib.check(lib.mmb_split_tf32(_lib.ptr(Bf), _lib.ptr(hi), _lib.ptr(lo), Bf.numel(),
+                                  _lib.stream_of(Bf)), "mmb_split_tf32")
+    assert torch.equal(hi + lo, Bf)
+    C = gemm(A, hi, M, N, K, a_mn, 0, B_lo=lo)
+    ref = Af.double().cpu() @ Bf.double().cpu().t()
+    assert rel(C.cpu(), ref) <= TOL
+
+
+@pytest.mark.parametrize("M,N", [(65536, 128), (1000, 36), (3, 260)])
+def test_col_dot_vs_float64(M, N):
+    from momentummamba_b200.tc_gemm import col_dot
+    g = torch.Generator(device=DEV).manual_seed(M + N)
+    X = torch.randn(M, N, device=DEV, generator=g)
+    Y = torch.randn(M, N, device=DEV, generator=g)
+    out = col_dot(X, Y)
+    ref = (X.double() * Y.double()).sum(0).cpu()
+    assert rel(out.cpu(), ref) <= TOL
