@@ -78,9 +78,10 @@ __device__ __forceinline__ void umma_commit(uint64_t* bar) {
             smem_u32(bar))
         : "memory");
 }
-// 32 consecutive 32-bit columns of this thread's TMEM lane
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
-    uint32_t r[32];
+// 32 consecutive 32-bit columns of this thread's TMEM lane: the load, and the
+// wait that makes them readable (the registers pass through the wait, so no
+// use can be scheduled before it)
+__device__ __forceinline__ void tmem_ld32_issue(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
         "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
         "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
@@ -92,7 +93,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
           "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
           "=r"(r[31])
         : "r"(taddr));
-    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_wait32(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                   "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                   "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                   "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    tmem_ld32_issue(taddr, r);
+    tmem_wait32(r);
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
@@ -214,7 +230,7 @@ __device__ __forceinline__ void tg_split(float* hi, float* lo, int tid) {
 // BLO: B arrives split (B = its tf32 high parts, maps.blo its remainders), as
 // weights split once per call are: only A is split per tile.
 template <int BN, bool A_MN, bool B_MN, bool BLO>
-__global__ void __launch_bounds__(TG_NT)
+__global__ void __launch_bounds__(TG_NT, 1)
     tc_gemm_kernel(const TGParams p, const __grid_constant__ TGMaps maps) {
     using Sm = TGSmem<BN>;
     extern __shared__ float4 tg_smem4[];
@@ -325,12 +341,22 @@ __global__ void __launch_bounds__(TG_NT)
         // swizzle, and lane 0 stores (or adds) them with TMA; out-of-range rows
         // and columns are clipped by the copy
         float* wb = smem + warp * 2 * 1024;
-#pragma unroll 1
+        // the next 32 columns leave TMEM while this box is staged and stored
+        const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+        uint32_t rr[2][32];
+        tmem_ld32_issue(trow, rr[0]);
+        tmem_wait32(rr[0]);
+        // column boxes inside N (uniform across the CTA)
+        const int64_t ncols = p.N - n0 < BN ? p.N - n0 : BN;
+#pragma unroll
         for (int c = 0; c < BN; c += 32) {
+            const int cur = (c >> 5) & 1;
+            if (c >= ncols) continue;
+            if (c + 32 < ncols) tmem_ld32_issue(trow + (uint32_t)(c + 32), rr[cur ^ 1]);
             float v[32];
-            tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)c, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(rr[cur][j]);
             const int64_t nb = n0 + c;
-            if (nb >= p.N) break;  // uniform across the CTA
             if (p.E && mok) {
                 const float* er = p.E + m * p.lde;
 #pragma unroll
@@ -350,6 +376,7 @@ __global__ void __launch_bounds__(TG_NT)
                 tma_store_2d(&maps.c, buf, (int)nb, (int)(m0 + warp * 32), p.accumulate != 0);
                 bulk_commit();
             }
+            if (c + 32 < ncols) tmem_wait32(rr[cur ^ 1]);
         }
         if (lane == 0) bulk_wait_read<0>();
         __syncwarp();
