@@ -13,8 +13,8 @@
 // 2^-22 relative) -- close to a plain fp32 GEMM, unlike one-pass tf32 (2^-11).
 //
 // Tile: 128 x BN (BN = 128 or 256) per CTA, K in steps of 16 (one 64-byte
-// swizzle row of fp32 for K-major operands), two pipeline stages: 48 KB of
-// shared memory per stage at BN = 256, so two CTAs share an SM and one's
+// swizzle row of fp32 for K-major operands), two pipeline stages (48 KB each
+// at BN = 256, 32 KB at BN = 128), so two CTAs share an SM and one's
 // epilogue overlaps the other's loads (32-value K steps, one CTA per SM,
 // measured 118 us for M=65536 N=512 K=128).  Thread 0 issues the TMA copies
 // (raw fp32 tiles, 128-byte swizzle) and the MMAs; all 128 threads split the
@@ -28,13 +28,19 @@ namespace mmb {
 constexpr int TG_BM = 128;
 constexpr int TG_BK = 16;
 constexpr int TG_NT = 128;
-#ifndef MMB_TG_STAGES
-#define MMB_TG_STAGES 2
+// Pipeline stages of 128-column tiles (256-column tiles keep 2: three would
+// leave one CTA per SM).  Three stages (the producer refills the stage of tile
+// i - 2 while tile i - 1's MMAs still run) measured the same as two (85 us for
+// M=65536 N=128 K=512): each tile's A still waits out a DRAM round trip, the
+// prefetch being one tile deep either way.
+#ifndef MMB_TG_STAGES_N128
+#define MMB_TG_STAGES_N128 2
 #endif
 #ifndef MMB_TG_BN_MAX
 #define MMB_TG_BN_MAX 256
 #endif
-constexpr int TG_STAGES = MMB_TG_STAGES;
+template <int BN>
+__host__ __device__ constexpr int tg_stages() { return BN == 128 ? MMB_TG_STAGES_N128 : 2; }
 constexpr uint32_t TG_MASK_HI = 0xffffe000u;  // fp32 bits kept by tf32
 
 // ---------------------------------------------------------------------------
@@ -184,7 +190,7 @@ struct TGSmem {
     static constexpr int B_FLOATS = BN * TG_BK;
     // per stage: A_hi | A_lo | B_hi | B_lo (each 1024-byte aligned)
     static constexpr int STAGE = 2 * A_FLOATS + 2 * B_FLOATS;
-    static constexpr size_t BYTES = (size_t)TG_STAGES * STAGE * 4 + 1024;
+    static constexpr size_t BYTES = (size_t)tg_stages<BN>() * STAGE * 4 + 1024;
 };
 
 // Load one 128 x 16 (A) or BN x 16 (B) fp32 tile.  K-major: one box of 16 (K)
@@ -234,6 +240,7 @@ __global__ void __launch_bounds__(TG_NT, 1)
     tc_gemm_kernel(const TGParams p, const __grid_constant__ TGMaps maps) {
     using Sm = TGSmem<BN>;
     extern __shared__ float4 tg_smem4[];
+    constexpr int TG_STAGES = tg_stages<BN>();
     __shared__ uint64_t tma_bar[TG_STAGES], mma_bar[TG_STAGES];
     __shared__ uint32_t tmem_base_s;
     float* smem = reinterpret_cast<float*>(
@@ -277,11 +284,12 @@ __global__ void __launch_bounds__(TG_NT, 1)
     if (tid == 0 && nk > 0) issue(0);
     for (int i = 0; i < nk; ++i) {
         const int s = i % TG_STAGES;
-        // thread 0: the next tile goes into the other stage once the MMAs that
-        // read it (tile i - 1) are done
+        // thread 0: the next tile goes into its stage once the MMAs of the tile
+        // that stage last held (i + 1 - STAGES) are done
         if (tid == 0 && i + 1 < nk) {
-            if (i >= 1) ok = mbar_wait_bounded(&mma_bar[(i - 1) % TG_STAGES],
-                                               (uint32_t)(((i - 1) / TG_STAGES) & 1));
+            const int prev = i + 1 - TG_STAGES;
+            if (prev >= 0) ok = mbar_wait_bounded(&mma_bar[prev % TG_STAGES],
+                                                  (uint32_t)((prev / TG_STAGES) & 1));
             if (ok) issue(i + 1);
         }
         if (ok) ok = mbar_wait_bounded(&tma_bar[s], (uint32_t)((i / TG_STAGES) & 1));
