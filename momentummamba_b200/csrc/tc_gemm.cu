@@ -33,6 +33,14 @@ constexpr int TG_NT = 128;
 // i - 2 while tile i - 1's MMAs still run) measured the same as two (85 us for
 // M=65536 N=128 K=512): each tile's A still waits out a DRAM round trip, the
 // prefetch being one tile deep either way.
+// The warp-specialised persistent kernel (1) or the one-role-per-phase kernel
+// with two CTAs per SM (0); SMs the persistent grid covers.
+#ifndef MMB_TG_WS
+#define MMB_TG_WS 1
+#endif
+#ifndef MMB_TG_SMS
+#define MMB_TG_SMS 148
+#endif
 #ifndef MMB_TG_STAGES_N128
 #define MMB_TG_STAGES_N128 2
 #endif
@@ -152,6 +160,7 @@ struct TGParams {
     const float* evec;
     int accumulate;  // 1: C += (vector reductions; split-K), 0: C =
     int tma_c;       // C goes out through 32 x 32 TMA boxes (aligned C)
+    int e_vec;       // E and evec 16-byte aligned with lde % 4 == 0: vector loads
     int* err;
 };
 struct TGMaps {
@@ -429,6 +438,294 @@ __global__ void __launch_bounds__(TG_NT, 1)
     }
 }
 
+// ---------------------------------------------------------------------------
+// Warp-specialised, persistent variant: one CTA per SM walks its tiles with
+// the roles in separate warps, so loads, splits, MMAs and the epilogue of
+// consecutive K-blocks and tiles overlap:
+//   warp 0      TMA producer: raw tiles into a ring of WS_RING slots, up to
+//               the ring's depth ahead (a slot is refilled once the MMAs that
+//               read it have completed);
+//   warp 1      TMEM owner and MMA issuer: two accumulators of BN columns, so
+//               tile t + 1 accumulates while the epilogue drains tile t;
+//   warps 2-5   split each landed tile in place into tf32 high parts and
+//               remainders (A, and B unless it came split);
+//   warps 6-9   epilogue: TMEM -> registers -> 32 x 32 boxes in shared memory
+//               -> TMA store (or reduce-add for K slices).
+// Every wait is bounded; a wait that gives up raises a CTA-wide abort flag
+// that the other roles' waits see, the MMAs in flight are drained and TMEM is
+// freed before the CTA leaves.
+// ---------------------------------------------------------------------------
+constexpr int WS_SPLIT_WARPS = 4;
+constexpr int WS_SPLIT_THREADS = 32 * WS_SPLIT_WARPS;
+constexpr int WS_NT = 32 * (2 + WS_SPLIT_WARPS + 4);
+// Ring depth: the raw tiles in flight per SM are what hides the DRAM latency.
+template <int BN>
+__host__ __device__ constexpr int ws_ring() { return BN == 256 ? 3 : 6; }
+
+template <int BN>
+struct WSSmem {
+    static constexpr int A_FLOATS = TG_BM * TG_BK;
+    static constexpr int B_FLOATS = BN * TG_BK;
+    static constexpr int SLOT = 2 * A_FLOATS + 2 * B_FLOATS;  // A_hi | A_lo | B_hi | B_lo
+    static constexpr int EPI = 4 * 2 * 1024;                   // 2 staging boxes per epilogue warp
+    static constexpr size_t BYTES = (size_t)(ws_ring<BN>() * SLOT + EPI) * 4 + 1024;
+};
+
+// Bounded wait on phase `parity` that also gives up when another role aborted.
+__device__ __forceinline__ bool ws_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                        int* err) {
+    for (int i = 0; i < MMB_WAIT_POLLS; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+    }
+    *abort = 1;
+    if (err) atomicOr(err, 1);
+    return false;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+template <int BN, bool A_MN, bool B_MN, bool BLO>
+__global__ void __launch_bounds__(WS_NT, 1)
+    tc_gemm_ws_kernel(const TGParams p, const __grid_constant__ TGMaps maps) {
+    using Sm = WSSmem<BN>;
+    constexpr int R = ws_ring<BN>();
+    constexpr uint32_t IDESC = tf32_idesc(BN, A_MN, B_MN);
+    constexpr uint32_t TX = (uint32_t)(TG_BM + (BLO ? 2 : 1) * BN) * TG_BK * 4;
+    extern __shared__ float4 ws_smem4[];
+    __shared__ uint64_t full[R], split[R], empty[R], acc_full[2], acc_empty[2], drained;
+    __shared__ uint32_t tmem_base_s;
+    __shared__ int abort_s;
+    volatile int* abort = &abort_s;
+    float* smem = reinterpret_cast<float*>(
+        (reinterpret_cast<uintptr_t>(ws_smem4) + 1023) & ~(uintptr_t)1023);
+    float* epi = smem + R * Sm::SLOT;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    const int64_t mt = (p.M + TG_BM - 1) / TG_BM, nt = (p.N + BN - 1) / BN;
+    const int64_t nz = (p.K + p.kchunk - 1) / p.kchunk;
+    const int64_t ntiles = mt * nt * nz;
+    // tile t: m fastest (consecutive CTAs share the B panel in L2), then n, then K slice
+    auto tile_of = [&](int64_t t, int64_t& m0, int64_t& n0, int64_t& kb, int& nk) {
+        const int64_t z = t / (mt * nt), r = t % (mt * nt);
+        m0 = (r % mt) * TG_BM;
+        n0 = (r / mt) * BN;
+        kb = z * p.kchunk;
+        const int64_t ke = min64(p.K, kb + p.kchunk);
+        nk = (int)((ke - kb + TG_BK - 1) / TG_BK);
+    };
+    auto slot_a = [&](int s) { return smem + s * Sm::SLOT; };
+    auto slot_alo = [&](int s) { return smem + s * Sm::SLOT + Sm::A_FLOATS; };
+    auto slot_b = [&](int s) { return smem + s * Sm::SLOT + 2 * Sm::A_FLOATS; };
+    auto slot_blo = [&](int s) { return smem + s * Sm::SLOT + 2 * Sm::A_FLOATS + Sm::B_FLOATS; };
+
+    if (tid == 0) {
+        abort_s = 0;
+        for (int s = 0; s < R; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&split[s], WS_SPLIT_THREADS);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 128);
+        }
+        mbar_init(&drained, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) tmem_alloc(&tmem_base_s, 2 * BN);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base_s;
+
+    if (warp == 0) {
+        // ---- producer ----
+        if (lane == 0) {
+            int64_t j = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+                int64_t m0, n0, kb;
+                int nk;
+                tile_of(t, m0, n0, kb, nk);
+                for (int k = 0; k < nk && ok; ++k, ++j) {
+                    const int s = (int)(j % R);
+                    if (j >= R) ok = ws_wait(&empty[s], (uint32_t)(((j / R) - 1) & 1), abort, p.err);
+                    if (!ok) break;
+                    const int64_t k0 = kb + (int64_t)k * TG_BK;
+                    mbar_expect_tx(&full[s], TX);
+                    tg_load<TG_BM, A_MN>(slot_a(s), &maps.a, m0, k0, &full[s]);
+                    tg_load<BN, B_MN>(slot_b(s), &maps.b, n0, k0, &full[s]);
+                    if constexpr (BLO) tg_load<BN, B_MN>(slot_blo(s), &maps.blo, n0, k0, &full[s]);
+                }
+            }
+            // copies still in flight land before the CTA leaves
+            for (int64_t q = j - R > 0 ? j - R : 0; q < j; ++q)
+                mbar_wait_polls(&full[q % R], (uint32_t)((q / R) & 1), 1 << 16);
+        }
+    } else if (warp == 1) {
+        // ---- MMA issuer ----
+        if (lane == 0) {
+            int64_t j = 0, lt = 0;
+            bool ok = true;
+            for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++lt) {
+                int64_t m0, n0, kb;
+                int nk;
+                tile_of(t, m0, n0, kb, nk);
+                const int a = (int)(lt & 1);
+                if (lt >= 2) ok = ws_wait(&acc_empty[a], (uint32_t)(((lt / 2) - 1) & 1), abort, p.err);
+                if (!ok) break;
+                tc_fence_after();
+                const uint32_t acc = tmem + (uint32_t)(a * BN);
+                for (int k = 0; k < nk && ok; ++k, ++j) {
+                    const int s = (int)(j % R);
+                    ok = ws_wait(&split[s], (uint32_t)((j / R) & 1), abort, p.err);
+                    if (!ok) break;
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < TG_BK / 8; ++kk) {
+                        const uint64_t ah = tg_desc<TG_BM, A_MN>(slot_a(s), kk);
+                        const uint64_t al = tg_desc<TG_BM, A_MN>(slot_alo(s), kk);
+                        const uint64_t bh = tg_desc<BN, B_MN>(slot_b(s), kk);
+                        const uint64_t bl = tg_desc<BN, B_MN>(slot_blo(s), kk);
+                        umma_tf32(acc, ah, bh, IDESC, (k > 0 || kk > 0) ? 1u : 0u);
+                        umma_tf32(acc, ah, bl, IDESC, 1u);
+                        umma_tf32(acc, al, bh, IDESC, 1u);
+                    }
+                    umma_commit(&empty[s]);
+                }
+                if (ok) umma_commit(&acc_full[a]);
+            }
+            // every MMA this CTA issued has completed before TMEM is freed
+            umma_commit(&drained);
+            mbar_wait_polls(&drained, 0, 1 << 20);
+        }
+    } else if (warp < 2 + WS_SPLIT_WARPS) {
+        // ---- splitters ----
+        const int st = tid - 64;
+        int64_t j = 0;
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x) {
+            int64_t m0, n0, kb;
+            int nk;
+            tile_of(t, m0, n0, kb, nk);
+            for (int k = 0; k < nk && ok; ++k, ++j) {
+                const int s = (int)(j % R);
+                ok = ws_wait(&full[s], (uint32_t)((j / R) & 1), abort, p.err);
+                if (!ok) break;
+#pragma unroll 4
+                for (int i = st; i < Sm::A_FLOATS / 4; i += WS_SPLIT_THREADS) {
+                    const float4 x = reinterpret_cast<float4*>(slot_a(s))[i];
+                    float4 h, l;
+                    h.x = __uint_as_float(__float_as_uint(x.x) & TG_MASK_HI);
+                    h.y = __uint_as_float(__float_as_uint(x.y) & TG_MASK_HI);
+                    h.z = __uint_as_float(__float_as_uint(x.z) & TG_MASK_HI);
+                    h.w = __uint_as_float(__float_as_uint(x.w) & TG_MASK_HI);
+                    l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
+                    reinterpret_cast<float4*>(slot_a(s))[i] = h;
+                    reinterpret_cast<float4*>(slot_alo(s))[i] = l;
+                }
+                if constexpr (!BLO) {
+#pragma unroll 4
+                    for (int i = st; i < Sm::B_FLOATS / 4; i += WS_SPLIT_THREADS) {
+                        const float4 x = reinterpret_cast<float4*>(slot_b(s))[i];
+                        float4 h, l;
+                        h.x = __uint_as_float(__float_as_uint(x.x) & TG_MASK_HI);
+                        h.y = __uint_as_float(__float_as_uint(x.y) & TG_MASK_HI);
+                        h.z = __uint_as_float(__float_as_uint(x.z) & TG_MASK_HI);
+                        h.w = __uint_as_float(__float_as_uint(x.w) & TG_MASK_HI);
+                        l.x = x.x - h.x; l.y = x.y - h.y; l.z = x.z - h.z; l.w = x.w - h.w;
+                        reinterpret_cast<float4*>(slot_b(s))[i] = h;
+                        reinterpret_cast<float4*>(slot_blo(s))[i] = l;
+                    }
+                }
+                fence_proxy_async_smem();
+                mbar_arrive(&split[s]);
+            }
+        }
+    } else {
+        // ---- epilogue: warp q = warp % 4 reads TMEM lanes 32q..32q+31 (the four
+        // epilogue warps cover the four lane quarters) ----
+        const int q = warp & 3;
+        float* wb = epi + q * 2 * 1024;
+        int64_t lt = 0;
+        int nbox = 0;  // boxes this warp has stored (staging buffer parity)
+        bool ok = true;
+        for (int64_t t = blockIdx.x; t < ntiles && ok; t += gridDim.x, ++lt) {
+            int64_t m0, n0, kb;
+            int nk;
+            tile_of(t, m0, n0, kb, nk);
+            const int a = (int)(lt & 1);
+            ok = ws_wait(&acc_full[a], (uint32_t)((lt / 2) & 1), abort, p.err);
+            if (!ok) break;
+            tc_fence_after();
+            const int64_t m = m0 + q * 32 + lane;
+            const bool mok = m < p.M;
+            const int64_t ncols = p.N - n0 < BN ? p.N - n0 : BN;
+            const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(a * BN);
+            uint32_t rr[2][32];
+            tmem_ld32_issue(trow, rr[0]);
+            tmem_wait32(rr[0]);
+#pragma unroll
+            for (int c = 0; c < BN; c += 32) {
+                const int cur = (c >> 5) & 1;
+                if (c >= ncols) continue;
+                if (c + 32 < ncols) tmem_ld32_issue(trow + (uint32_t)(c + 32), rr[cur ^ 1]);
+                float v[32];
+#pragma unroll
+                for (int jj = 0; jj < 32; ++jj) v[jj] = __uint_as_float(rr[cur][jj]);
+                const int64_t nb = n0 + c;
+                if (p.E && mok) {
+                    const float* er = p.E + m * p.lde + nb;
+                    if (p.e_vec && nb + 32 <= p.N) {
+                        // whole 32-column box of an aligned E: vector loads
+#pragma unroll
+                        for (int jj = 0; jj < 32; jj += 4) {
+                            const float4 e4 = *reinterpret_cast<const float4*>(er + jj);
+                            const float4 w4 = *reinterpret_cast<const float4*>(p.evec + nb + jj);
+                            v[jj] = fmaf(w4.x, e4.x, v[jj]);
+                            v[jj + 1] = fmaf(w4.y, e4.y, v[jj + 1]);
+                            v[jj + 2] = fmaf(w4.z, e4.z, v[jj + 2]);
+                            v[jj + 3] = fmaf(w4.w, e4.w, v[jj + 3]);
+                        }
+                    } else {
+#pragma unroll
+                        for (int jj = 0; jj < 32; ++jj)
+                            if (nb + jj < p.N) v[jj] = fmaf(p.evec[nb + jj], er[jj], v[jj]);
+                    }
+                }
+                float* buf = wb + (nbox & 1) * 1024;
+                if (lane == 0) bulk_wait_read<1>();
+                __syncwarp();
+#pragma unroll
+                for (int jj = 0; jj < 8; ++jj)
+                    reinterpret_cast<float4*>(buf + lane * 32)[jj ^ (lane & 7)] =
+                        make_float4(v[4 * jj], v[4 * jj + 1], v[4 * jj + 2], v[4 * jj + 3]);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    tma_store_2d(&maps.c, buf, (int)nb, (int)(m0 + q * 32), p.accumulate != 0);
+                    bulk_commit();
+                }
+                ++nbox;
+                if (c + 32 < ncols) tmem_wait32(rr[cur ^ 1]);
+            }
+            // this warp's reads of the accumulator are done: it may be refilled
+            tc_fence_before();
+            mbar_arrive(&acc_empty[a]);
+        }
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, 2 * BN);
+    }
+}
+
 template <int BN, bool A_MN, bool B_MN, bool BLO>
 static int tg_launch(const TGParams& p0, const float* A, int64_t lda, const float* B,
                      const float* Blo, int64_t ldb, int splits, cudaStream_t s) {
@@ -451,11 +748,24 @@ static int tg_launch(const TGParams& p0, const float* A, int64_t lda, const floa
     p.tma_c = (((uintptr_t)p.C & 15) == 0 && (p.ldc & 3) == 0 &&
                mmb_encode_tile_map(&maps.c, p.C, 4, p.N, p.M, 1, p.ldc, p.ldc * p.M, 32, 32, 128))
                   ? 1 : 0;
+    p.err = mmb_device_error_flag();
+    p.e_vec = p.E && ((uintptr_t)p.E & 15) == 0 && ((uintptr_t)p.evec & 15) == 0 &&
+              (p.lde & 3) == 0;
+    if (MMB_TG_WS && p.tma_c) {
+        // persistent: one CTA per SM over all (m, n, K-slice) tiles
+        static int attr_ws[MMB_MAX_DEVICES] = {};
+        const int st =
+            mmb_smem_attr(tc_gemm_ws_kernel<BN, A_MN, B_MN, BLO>, WSSmem<BN>::BYTES, attr_ws);
+        if (st != MMB_OK) return st;
+        const int64_t tiles = (p.M + TG_BM - 1) / TG_BM * ((p.N + BN - 1) / BN) * splits;
+        const unsigned grid = (unsigned)(tiles < MMB_TG_SMS ? tiles : MMB_TG_SMS);
+        tc_gemm_ws_kernel<BN, A_MN, B_MN, BLO><<<grid, WS_NT, WSSmem<BN>::BYTES, s>>>(p, maps);
+        return mmb_launch_status();
+    }
     static int attr_done[MMB_MAX_DEVICES] = {};
     const int st =
         mmb_smem_attr(tc_gemm_kernel<BN, A_MN, B_MN, BLO>, TGSmem<BN>::BYTES, attr_done);
     if (st != MMB_OK) return st;
-    p.err = mmb_device_error_flag();
     dim3 grid((unsigned)((p.M + TG_BM - 1) / TG_BM), (unsigned)((p.N + BN - 1) / BN),
               (unsigned)splits);
     tc_gemm_kernel<BN, A_MN, B_MN, BLO><<<grid, TG_NT, TGSmem<BN>::BYTES, s>>>(p, maps);
