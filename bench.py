@@ -903,9 +903,9 @@ def run_linoss_layer(ctx, steps):
     ms_cu, _ = timed_region(ctx, step_cublas, max(3, steps // 4))
     ms_cu *= steps / max(3, steps // 4)
     # one of the four tensor-core GEMM shapes alone: Bu = u Bm^T (M = B L, N = 2P, K = H)
-    from momentummamba_b200.tc_gemm import gemm_nt
+    from momentummamba_b200.tc_gemm import gemm_nt, split_tf32
     u2 = u.detach().reshape(Bsz * L, H)
-    Bm = torch.randn(2 * P, H, device=dev)
+    Bm = split_tf32(torch.randn(2 * P, H, device=dev))   # as the layer: weights split once
     t = launch_times((("tc_gemm Bu", lambda: gemm_nt(u2, Bm)),))
     del layers, u, gy, u2, Bm
     torch.cuda.empty_cache()
@@ -925,7 +925,8 @@ def run_linoss_layer(ctx, steps):
                    "parallelism": f"batch-sharded x{world}", "launch": "eager (autograd)",
                    "l2": "inputs larger than L2 (Bu, x2 134 MB each)"},
         "cublas_contractions_ms_per_step": ms_cu / steps,
-        "roofline": {"kernel": "tc_gemm_kernel (Bu = u Bm^T, M=65536 N=512 K=128)",
+        "roofline": {"kernel": "tc_gemm_ws_kernel (Bu = u Bm^T, M=65536 N=512 K=128, "
+                               "weights split once)",
                      "bound": "hbm", "achieved": achieved, "peak": peak,
                      "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s", "frac": achieved / peak,
                      "algorithmic_bytes": gemm_b, "ms_per_launch": t["tc_gemm Bu"],
