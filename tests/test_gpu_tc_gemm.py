@@ -150,3 +150,28 @@ def test_col_dot_vs_float64(M, N):
     out = col_dot(X, Y)
     ref = (X.double() * Y.double()).sum(0).cpu()
     assert rel(out.cpu(), ref) <= TOL
+
+
+@pytest.mark.parametrize("b_mn", [0, 1])
+def test_unaligned_c_takes_the_per_tile_kernel(b_mn):
+    """C rows of 130 floats cannot be stored by TMA boxes: the one-CTA-per-tile
+    kernel with direct stores runs instead, with the same result."""
+    M, N, K = 300, 130, 64
+    g = torch.Generator(device=DEV).manual_seed(31)
+    Af = torch.randn(M, K, device=DEV, generator=g)
+    Bf = torch.randn(N, K, device=DEV, generator=g)
+    if b_mn:
+        B = torch.zeros(K, 132, device=DEV)
+        B[:, :N] = Bf.t()
+    else:
+        B = Bf
+    C = gemm(Af, B, M, N, K, 0, b_mn)
+    ref = Af.double().cpu() @ Bf.double().cpu().t()
+    assert C.stride(0) == 130
+    assert rel(C.cpu(), ref) <= TOL
+    # and as a K-sliced reduction into an unaligned C
+    Bt = torch.zeros(K, 132, device=DEV)  # MN-major rows keep a 16-byte pitch
+    Bt[:, :N] = Bf.t()
+    C2 = torch.zeros(M, N, device=DEV)
+    gemm(Af.t().contiguous(), Bt, M, N, K, 1, 1, C=C2, accumulate=1, splits=3)
+    assert rel(C2.cpu(), ref) <= TOL
