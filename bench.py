@@ -390,6 +390,7 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
     fb, bb = fwd_bytes(Bsz, L, D, N), bwd_bytes(Bsz, L, D, N)
     achieved = bb / (t_bwd / 1e3) / 1e9
     traffic = load_traffic("mmscan_bwd_traffic.json", name)
+    kb = bwd_kernel_name(Bsz, D, N, nch)
     workload = (f"{NL}-layer momentum-Mamba scan fwd+bwd (expand 2, d_state {N}): "
                 f"B={Btot} L={L} D={D} N={N} per layer, softplus(delta+bias) and SiLU(z) "
                 f"gate fused, fp32")
@@ -410,8 +411,8 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
                    "l2": f"inputs larger than L2: {NL} layers x "
                          f"{fwd_bytes(Bsz, L, D, N) / 1e6:.0f} MB of scan inputs per step"},
         "roofline": {
-            "kernel": (f"mmscan_bwd_kernel<{N}>" if nch == 1 else
-                       f"backward call: clearing + summary + carry + mmscan_bwd_kernel<{N}> "
+            "kernel": (kb if nch == 1 else
+                       f"backward call: clearing + summary + carry + {kb} "
                        f"over {nch} time chunks"),
             "bound": "hbm", "achieved": achieved,
             "peak": peak, "peak_kind": f"{peak_kind} hbm_gbs", "unit": "GB/s",
@@ -424,7 +425,7 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
             f"mmscan_fwd_kernel<{N}>": {"ms": t_fwd, "algorithmic_bytes": fb,
                                         "GB/s": fb / (t_fwd / 1e3) / 1e9,
                                         "frac": fb / (t_fwd / 1e3) / 1e9 / peak},
-            f"mmscan_bwd_kernel<{N}>": {"ms": t_bwd, "algorithmic_bytes": bb,
+            kb: {"ms": t_bwd, "algorithmic_bytes": bb,
                                         "GB/s": achieved, "frac": achieved / peak},
         },
         "hbm_gbs_step": NL * (fb + bb) * steps / (ms / 1e3) / 1e9,
@@ -437,6 +438,16 @@ def run_stack(ctx, cfg, strong, steps, with_e2e, with_cpu, name):
         "clocks": clocks,
         "cpu_baseline": cpu,
     }
+
+
+def bwd_kernel_name(Bsz, D, N, nch):
+    """The backward kernel the library picks for an fp32 call with 4 states per
+    thread: the two-channel kernel (256 / N channels per one-warp CTA) when its
+    grid gives every one of the 148 SMs at least 6 CTAs, else the one-channel
+    kernel."""
+    ctas = -(-D // (256 // N)) * Bsz * nch
+    two = 8 <= N <= 32 and ctas >= 148 * 6
+    return f"mmscan_bwd2_kernel<{N}>" if two else f"mmscan_bwd_kernel<{N}>"
 
 
 def chunk_len(lib, _lib, desc):

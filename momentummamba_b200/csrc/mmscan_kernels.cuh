@@ -21,6 +21,11 @@
 // channel's partial sums of y = C h are reduce-scattered so each lane finishes
 // its own items.
 //
+// Wide backward grids use mmscan_bwd2_kernel instead: a thread owns 4 states
+// of two channels, so each B / C value it loads serves both and the pair's dB |
+// dC terms are summed in registers (about half the shared-memory traffic per
+// element), with each 8-step window replayed in halves to fit the registers.
+//
 // The forward stores (h, v) every 8 steps as checkpoints.  The backward walks
 // the sequence in reverse, 8 steps at a time: it recomputes the window forward
 // from its checkpoint into registers (a_t and h_t), then runs the adjoint
@@ -62,7 +67,8 @@ constexpr int MM_NS = MMB_MM_STAGES;
 
 __host__ __device__ constexpr int ilog2c(int v) { return v <= 1 ? 0 : 1 + ilog2c(v / 2); }
 
-template <int N, int NP, int NT = MM_NT, int TS = MM_T>
+// DP: channels per thread (1; 2 in the two-channel backward).
+template <int N, int NP, int NT = MM_NT, int TS = MM_T, int DP = 1>
 struct MMCfg {
     static constexpr int NTH = NT;                    // threads per CTA
     static constexpr int T = TS;                      // steps per staged chunk
@@ -71,8 +77,8 @@ struct MMCfg {
     static constexpr int LOG2G = ilog2c(G);
     static constexpr int LB = LOG2G < 3 ? LOG2G : 3;  // lane bits that split an 8-step block
     static constexpr int IPL = MM_CK >> LB;           // (t, d) items a lane owns per block
-    static constexpr int DT = NT / G;                 // channels per CTA
-    static constexpr int DPW = 32 / G;                // channels per warp
+    static constexpr int DT = NT / G * DP;            // channels per CTA
+    static constexpr int DPW = 32 / G * DP;           // channels per warp
     static constexpr int LOG2DPW = 5 - LOG2G;
     // (T x DT) fp32 activation tile: dense rows of DT floats whose 16-byte
     // chunks are XOR-swizzled across rows -- the TMA swizzle of a DT*4-byte row
@@ -97,9 +103,9 @@ struct MMCfg {
 // kernel widens.  Stages start on 1024-byte boundaries (the swizzle period);
 // MM_SMEM_ALIGN bytes of slack let the kernel align its dynamic base.
 constexpr int MM_SMEM_ALIGN = 1024;
-template <int N, int NP, int NDT, int EBYTES, int NT = MM_NT, int TS = MM_T>
+template <int N, int NP, int NDT, int EBYTES, int NT = MM_NT, int TS = MM_T, int DP = 1>
 struct MMSmem {
-    using Cf = MMCfg<N, NP, NT, TS>;
+    using Cf = MMCfg<N, NP, NT, TS, DP>;
     static constexpr bool WIDE = EBYTES == 2;
     static constexpr int F32 = NDT * Cf::TR + 2 * Cf::TN;             // floats per fp32 stage
     static constexpr int RAW = NDT * TS * Cf::DT + 2 * TS * N;        // 16-bit words per raw stage
@@ -298,10 +304,10 @@ __device__ __forceinline__ void ckpt_load(const float* src, float2 (&h)[NP / 2],
 // the tiles it is about to copy and issues one tensor copy per tile; the other
 // threads only wait on the barrier.  Otherwise every thread issues cp.async
 // copies and waits on its own groups.
-template <int N, int NP, int NDT, class E, int NT = MM_NT, int TS = MM_T>
+template <int N, int NP, int NDT, class E, int NT = MM_NT, int TS = MM_T, int DP = 1>
 struct MMStager {
-    using Cf = MMCfg<N, NP, NT, TS>;
-    using Sm = MMSmem<N, NP, NDT, E::BYTES, NT, TS>;
+    using Cf = MMCfg<N, NP, NT, TS, DP>;
+    using Sm = MMSmem<N, NP, NDT, E::BYTES, NT, TS, DP>;
     using ET = typename E::T;
     float* smem;      // aligned dynamic base
     uint64_t* bars;   // MM_NS transaction barriers
@@ -1053,6 +1059,400 @@ __global__ void __launch_bounds__(NT, (NT == 32 ? MMB_BWD_MIN_WARPS : 1))
 }
 
 // ---------------------------------------------------------------------------
+// backward, two channels per thread (one-warp CTAs, NP = 4, N = 8 / 16 / 32)
+//
+// The same adjoint as mmscan_bwd_kernel, with each thread owning NP = 4 states
+// of two channels: channel pr and pr + DT/2 of the CTA's tile (pr = the lane's
+// channel pair).  The B and C values a thread loads from shared memory serve
+// both channels, and the two channels' dB | dC terms are added in registers
+// before they go to the window buffer, whose rows are channel pairs: per scan
+// element the shared-memory traffic is about halved, and every step has twice
+// the independent FMA chains.  Both channels' window states do not fit in
+// registers at once, so a window is replayed in halves: steps 0-3 from the
+// checkpoint to the middle state; steps 4-7 from there, keeping (h, a) for
+// their adjoint; then steps 0-3 again, kept for theirs (1.5 replays per
+// window instead of one).  The adjoint carries lam = a_s gh_s, so that
+//   gh_s = dy_s C_s + lam_{s+1},   lam_s = a_s gh_s,   d a_s-term = lam_s h_{s-1}.
+// The n-sums of each half window are reduce-scattered so that each lane
+// finishes 8 / G of its pair's (step, channel) items.
+// ---------------------------------------------------------------------------
+template <int N, bool SOFTPLUS, bool HAS_Z, class E, int TS>
+__global__ void __launch_bounds__(32, MMB_BWD_MIN_WARPS)
+    mmscan_bwd2_kernel(const MMParams p, const __grid_constant__ MMTmaps tmaps) {
+    constexpr int NP = 4, NT = 32, NP2 = 2;
+    using Cf = MMCfg<N, NP, NT, TS, 2>;
+    using Sm = MMSmem<N, NP, 4, E::BYTES, NT, TS, 2>;
+    using ET = typename E::T;
+    constexpr int DT = Cf::DT, G = Cf::G, LG = Cf::LOG2G, T = TS, TR = Cf::TR;
+    constexpr int NPR = DT / 2;   // channel pairs of the CTA = window-buffer rows
+    constexpr int IH = 8 >> LG;   // (step, channel) items a lane owns per half window
+    constexpr int NQ = 2 * N / 4; // float4 columns per window-buffer row
+    constexpr int SWZ = NQ / 2;   // float4 swizzle of odd rows (= G units of NP floats)
+    static_assert(G >= 2 && G <= 8 && NPR * G == 32, "two-channel backward: N = 8, 16 or 32");
+    extern __shared__ float4 smem4[];
+    __shared__ uint64_t bars[MM_NS];
+    // tiles: x | delta | z | dout (T x DT), B | C (T x N); then the window buffer
+    MMStager<N, NP, 4, E, NT, TS, 2> stg{mm_smem_base(smem4), bars, &tmaps, (int)threadIdx.x, 0,
+                                         p.vec, p.tma};
+    mm_pipe_init(bars, p.tma);
+    float* wbuf = stg.smem + Sm::FLOATS;  // [8 steps][NPR][2N]
+
+    const int lane = threadIdx.x;
+    const int ng = lane & (G - 1);
+    const int lane_base = lane & ~(G - 1);
+    const int pr = lane >> LG;
+    const int ibase = rs_index<8, LG>(ng, 0);  // first item of this lane in a half window
+    const int64_t b = blockIdx.y;
+    const int64_t d0 = (int64_t)blockIdx.x * DT;
+    const int64_t dch0 = d0 + pr;  // channel 0 of the pair; channel 1 is NPR further
+    const bool dv0 = dch0 < p.D, dv1 = dch0 + NPR < p.D;
+    stg.dcols = (int)min64(DT, p.D - d0);
+    const MMRange rg = mm_range<true, TS>(p, b, dch0);
+    const int64_t te = rg.te;
+    const int swz_units = (pr & 1) ? G : 0;
+    const ET* gx = static_cast<const ET*>(p.x);
+    const ET* gdl = static_cast<const ET*>(p.delta);
+    const ET* gz = static_cast<const ET*>(p.z);
+    const ET* gdo = static_cast<const ET*>(p.dout);
+    const ET* gB = static_cast<const ET*>(p.Bm);
+    const ET* gC = static_cast<const ET*>(p.Cm);
+    ET* gdx = static_cast<ET*>(p.dx);
+    ET* gddl = static_cast<ET*>(p.ddelta);
+    ET* gdz = static_cast<ET*>(p.dz);
+
+    float2 A2[2][NP2], lam[2][NP2], gv[2][NP2], dA[2][NP2];
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+        const bool ok = c ? dv1 : dv0;
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) {
+            A2[c][j] = lam[c][j] = gv[c][j] = dA[c][j] = f2(0.f);
+            if (ok) {
+                const float* Ar = p.A + (dch0 + c * NPR) * N + ng * NP + 2 * j;
+                A2[c][j] = make_float2(Ar[0] * MMB_LOG2E, Ar[1] * MMB_LOG2E);
+            }
+        }
+        // the pair arriving from the step after the chunk: (a gh, gv) = (lam, gv)
+        if (p.gstate_in && ok) {
+            const float* s = p.gstate_in + (rg.rec + c * NPR) * (2 * N) + ng * NP;
+            ld_pairs_g<NP>(s, lam[c]);
+            ld_pairs_g<NP>(s + N, gv[c]);
+        }
+    }
+    const float bias0 = (p.dbias && dv0) ? p.dbias[dch0] : 0.f;
+    const float bias1 = (p.dbias && dv1) ? p.dbias[dch0 + NPR] : 0.f;
+    const float Dv0 = (p.Dskip && dv0) ? p.Dskip[dch0] : 0.f;
+    const float Dv1 = (p.Dskip && dv1) ? p.Dskip[dch0 + NPR] : 0.f;
+    const float alpha = p.alpha;
+    const float2 beta2 = f2(p.beta);
+    float accD0 = 0.f, accD1 = 0.f, accB0 = 0.f, accB1 = 0.f;
+    const int nchunks = rg.ce - rg.cb;
+    // checkpoint of the next window to process (both channels)
+    float2 ckh[2][NP2], ckv[2][NP2];
+#pragma unroll
+    for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) ckh[c][j] = ckv[c][j] = f2(0.f);
+    const int64_t ck_stride = p.D * (2 * N);
+    const int64_t nck = (p.L + MM_CK - 1) / MM_CK;
+    const float* ckp =
+        p.ckpt_in + ((b * nck + (te - 1) / MM_CK) * p.D + dch0) * (2 * N) + ng * 2 * NP;
+    auto ck_next = [&]() {
+        if (dv0) ckpt_load<NP>(ckp, ckh[0], ckv[0]);
+        if (dv1) ckpt_load<NP>(ckp + NPR * 2 * N, ckh[1], ckv[1]);
+        ckp -= ck_stride;
+    };
+
+    auto stage = [&](int slot, int c) {
+        const int64_t t0 = (int64_t)(rg.cb + c) * T;
+        const int rv = (int)min64(T, te - t0);
+        stg.begin(slot, HAS_Z ? 4 : 3, 2);
+        stg.tile_d(slot, 0, TM_X, d0, t0, b, gx + b * p.xs[0] + t0 * p.xs[1] + d0, p.xs[1], rv);
+        stg.tile_d(slot, 1, TM_DELTA, d0, t0, b, gdl + b * p.ds[0] + t0 * p.ds[1] + d0, p.ds[1],
+                   rv);
+        if (HAS_Z)
+            stg.tile_d(slot, 2, TM_Z, d0, t0, b, gz + b * p.zs[0] + t0 * p.zs[1] + d0, p.zs[1],
+                       rv);
+        stg.tile_d(slot, 3, TM_DOUT, d0, t0, b, gdo + (b * p.L + t0) * p.D + d0, p.D, rv);
+        stg.tile_n(slot, 0, TM_B, t0, b, gB + b * p.bs[0] + t0 * p.bs[1], p.bs[1], rv);
+        stg.tile_n(slot, 1, TM_C, t0, b, gC + b * p.cs[0] + t0 * p.cs[1], p.cs[1], rv);
+    };
+    constexpr unsigned DMASK = HAS_Z ? 15u : 11u;
+
+#pragma unroll
+    for (int it = 0; it < MM_NS - 1; ++it) {
+        if (it < nchunks) stage(it, nchunks - 1 - it);
+        stg.commit();
+    }
+    for (int it = 0; it < nchunks; ++it) {
+        const int c = nchunks - 1 - it;
+        if (it + MM_NS - 1 < nchunks) stage((it + MM_NS - 1) % MM_NS, c - (MM_NS - 1));
+        stg.commit();
+        const bool landed = stg.wait(it % MM_NS, it / MM_NS);
+        if (__syncthreads_or(!landed)) {
+            if (lane == 0 && p.err) atomicOr(p.err, 1);
+            return;
+        }
+        const float* st = stg.view(it % MM_NS, DMASK, 3u);
+        if (Sm::WIDE) __syncthreads();
+        const float* sx = st;
+        const float* sdl = st + TR;
+        const float* sz = st + 2 * TR;
+        const float* sdo = st + 3 * TR;
+        const float* sB = st + 4 * TR;
+        const float* sC = sB + Cf::TN;
+        const int64_t t0 = (int64_t)(rg.cb + c) * T;
+        const int Lc = (int)min64(T, te - t0);
+
+        for (int w = (Lc - 1) / MM_CK; w >= 0; --w) {
+            const int w0 = w * MM_CK;
+            if (it == 0 && w == (Lc - 1) / MM_CK) ck_next();
+            // this lane's items (half hf, i): item k = ibase + i of the half is
+            // step 4 hf + k / 2 of channel k % 2
+            float xi[2][IH], dti[2][IH], dyi[2][IH], gzi[2][IH], sgi[2][IH];
+            float dts[MM_CK][2], dtxs[MM_CK][2];
+            {
+                float dtxi[2][IH];
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+#pragma unroll
+                    for (int i = 0; i < IH; ++i) {
+                        const int k = ibase + i;
+                        const int ch = k & 1;
+                        const int row = Cf::dix(w0 + 4 * hf + (k >> 1), pr + ch * NPR);
+                        const float xv = sx[row];
+                        const float r = sdl[row] + (ch ? bias1 : bias0);
+                        float wv = 0.f;
+                        const float dt = SOFTPLUS ? softplus_w(r, wv) : r;
+                        xi[hf][i] = xv;
+                        dti[hf][i] = dt;
+                        dtxi[hf][i] = alpha * dt * xv;
+                        sgi[hf][i] = SOFTPLUS ? softplus_grad_w(r, wv) : 1.f;
+                        float dy = sdo[row];
+                        gzi[hf][i] = 0.f;
+                        if (HAS_Z) {
+                            const float zv = sz[row];
+                            const float sg = sigmoid_f(zv);
+                            gzi[hf][i] = dy * sg * (1.f + zv * (1.f - sg));
+                            dy *= zv * sg;
+                        }
+                        dyi[hf][i] = dy;
+                    }
+                }
+#pragma unroll
+                for (int s = 0; s < MM_CK; ++s) {
+#pragma unroll
+                    for (int ch = 0; ch < 2; ++ch) {
+                        const int k = 2 * (s & 3) + ch;
+                        const int src = lane_base | block_owner<LG>(k);
+                        dts[s][ch] = __shfl_sync(FULL, dti[s >> 2][k % IH], src);
+                        dtxs[s][ch] = __shfl_sync(FULL, dtxi[s >> 2][k % IH], src);
+                    }
+                }
+            }
+            // replay of steps [s0, s0 + 4) from (h, v); KEEP: hh[q + 1] = h after
+            // step s0 + q, aa[q] = a of that step
+            float2 hh[5][2][NP2], aa[4][2][NP2];
+            float2 h[2][NP2], v[2][NP2];
+            auto replay = [&](auto keep_tag, auto s0_tag) {
+                constexpr bool KEEP = decltype(keep_tag)::value;
+                constexpr int S0 = decltype(s0_tag)::value;
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const int s = S0 + q;
+                    float2 bq[NP2];
+                    ld_pairs<NP>(sB + (w0 + s) * N + ng * NP, bq);
+#pragma unroll
+                    for (int ch = 0; ch < 2; ++ch) {
+                        const float2 dtx2 = f2(dtxs[s][ch]);
+                        const float2 dt2 = f2(dts[s][ch]);
+#pragma unroll
+                        for (int j = 0; j < NP2; ++j) {
+                            const float2 e = fmul2(dt2, A2[ch][j]);
+                            const float2 a = make_float2(ex2(e.x), ex2(e.y));
+                            v[ch][j] = ffma2(beta2, v[ch][j], fmul2(dtx2, bq[j]));
+                            h[ch][j] = ffma2(a, h[ch][j], v[ch][j]);
+                            if (KEEP) {
+                                aa[q][ch][j] = a;
+                                hh[q + 1][ch][j] = h[ch][j];
+                            }
+                        }
+                    }
+                }
+            };
+            // adjoint of half HF (steps 4 HF + 3 .. 4 HF), its n-sums and items
+            auto adjoint = [&](auto half_tag) {
+                constexpr int HF = decltype(half_tag)::value;
+                float dys[4][2];
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+#pragma unroll
+                    for (int ch = 0; ch < 2; ++ch) {
+                        const int k = 2 * q + ch;
+                        dys[q][ch] = __shfl_sync(FULL, dyi[HF][k % IH], lane_base | block_owner<LG>(k));
+                    }
+                float yv[8], sab[16];
+#pragma unroll
+                for (int q = 3; q >= 0; --q) {
+                    const int s = 4 * HF + q;
+                    float2 bq[NP2], cq[NP2], pb[NP2], pc[NP2];
+                    ld_pairs<NP>(sB + (w0 + s) * N + ng * NP, bq);
+                    ld_pairs<NP>(sC + (w0 + s) * N + ng * NP, cq);
+#pragma unroll
+                    for (int ch = 0; ch < 2; ++ch) {
+                        if (HAS_Z) yv[2 * q + ch] = dot_pairs(cq, hh[q + 1][ch]);
+                        const float2 dy2 = f2(dys[q][ch]);
+                        const float2 dt2 = f2(dts[s][ch]);
+                        const float2 dtx2 = f2(dtxs[s][ch]);
+                        float2 sb = f2(0.f), sa = f2(0.f);
+#pragma unroll
+                        for (int j = 0; j < NP2; ++j) {
+                            const float2 gh = ffma2(dy2, cq[j], lam[ch][j]);
+                            gv[ch][j] = ffma2(beta2, gv[ch][j], gh);
+                            sb = ffma2(gv[ch][j], bq[j], sb);
+                            lam[ch][j] = fmul2(aa[q][ch][j], gh);
+                            const float2 t2 = fmul2(lam[ch][j], hh[q][ch][j]);
+                            sa = ffma2(t2, A2[ch][j], sa);
+                            dA[ch][j] = ffma2(t2, dt2, dA[ch][j]);
+                            pb[j] = ch ? ffma2(gv[ch][j], dtx2, pb[j]) : fmul2(gv[ch][j], dtx2);
+                            pc[j] = ch ? ffma2(dy2, hh[q + 1][ch][j], pc[j])
+                                       : fmul2(dy2, hh[q + 1][ch][j]);
+                        }
+                        sab[2 * (2 * q + ch)] = sa.x + sa.y;
+                        sab[2 * (2 * q + ch) + 1] = sb.x + sb.y;
+                    }
+                    // the pair's dB | dC terms of (step s, this lane's states)
+                    float4* r4 = reinterpret_cast<float4*>(wbuf + (s * NPR + pr) * 2 * N);
+                    r4[ng ^ swz_units] = make_float4(pb[0].x, pb[0].y, pb[1].x, pb[1].y);
+                    r4[(G + ng) ^ swz_units] = make_float4(pc[0].x, pc[0].y, pc[1].x, pc[1].y);
+                }
+                // n-sums back to the owning lanes: entry i = item ibase + i
+                if (HAS_Z) reduce_scatter<8, 0, LG>(yv, lane);
+                reduce_scatter<16, 0, LG>(sab, lane);
+#pragma unroll
+                for (int i = 0; i < IH; ++i) {
+                    const int k = ibase + i;
+                    const int ch = k & 1;
+                    const int64_t gt = t0 + w0 + 4 * HF + (k >> 1);
+                    const int64_t d = dch0 + ch * NPR;
+                    const int64_t gi = (b * p.L + gt) * p.D + d;
+                    const bool ok = (ch ? dv1 : dv0) && gt < te;
+                    const float SA = sab[2 * i] * MMB_LN2;
+                    const float SB = sab[2 * i + 1];
+                    const float xv = xi[HF][i];
+                    const float Dv = ch ? Dv1 : Dv0;
+                    if (HAS_Z) {
+                        const float gzv = gzi[HF][i] * fmaf(Dv, xv, yv[i]);
+                        if (ok && gdz) E::store(gdz, gi, gzv);
+                    }
+                    const float gdt = fmaf(alpha * xv, SB, SA) * sgi[HF][i];
+                    if (ok) {
+                        E::store(gdx, gi, fmaf(dyi[HF][i], Dv, alpha * dti[HF][i] * SB));
+                        E::store(gddl, gi, gdt);
+                        if (ch) {
+                            accD1 = fmaf(dyi[HF][i], xv, accD1);
+                            accB1 += gdt;
+                        } else {
+                            accD0 = fmaf(dyi[HF][i], xv, accD0);
+                            accB0 += gdt;
+                        }
+                    }
+                }
+            };
+            // steps 0-3 from the checkpoint to the middle state
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    h[ch][j] = ckh[ch][j];
+                    v[ch][j] = ckv[ch][j];
+                }
+            replay(std::false_type{}, std::integral_constant<int, 0>{});
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) hh[0][ch][j] = h[ch][j];
+            replay(std::true_type{}, std::integral_constant<int, 4>{});
+            adjoint(std::integral_constant<int, 1>{});
+            // steps 0-3 again, kept
+#pragma unroll
+            for (int ch = 0; ch < 2; ++ch)
+#pragma unroll
+                for (int j = 0; j < NP2; ++j) {
+                    h[ch][j] = ckh[ch][j];
+                    v[ch][j] = ckv[ch][j];
+                    hh[0][ch][j] = ckh[ch][j];
+                }
+            if (t0 + w0 > rg.tb) ck_next();  // the next (earlier) window's checkpoint
+            replay(std::true_type{}, std::integral_constant<int, 0>{});
+            adjoint(std::integral_constant<int, 0>{});
+            __syncwarp();
+            // d-sum of the window buffer over the NPR channel pairs: one vector
+            // reduction to global memory per (step, 4 columns)
+            {
+                constexpr int ITEMS = MM_CK * NQ;
+                constexpr int IPT = ITEMS / 32;
+                static_assert(ITEMS % 32 == 0, "window-buffer items per lane");
+#pragma unroll
+                for (int j = 0; j < IPT; ++j) {
+                    const int item = lane + j * 32;
+                    const int s = item / NQ, q = item % NQ;
+                    float2 acc01 = f2(0.f), acc23 = f2(0.f);
+#pragma unroll
+                    for (int r = 0; r < NPR; ++r) {
+                        const float4 vv = reinterpret_cast<const float4*>(
+                            wbuf + (s * NPR + r) * 2 * N)[q ^ ((r & 1) ? SWZ : 0)];
+                        acc01 = fadd2(acc01, make_float2(vv.x, vv.y));
+                        acc23 = fadd2(acc23, make_float2(vv.z, vv.w));
+                    }
+                    const int64_t gt = t0 + w0 + s;
+                    if (gt < te) {
+                        const int col = q * 4;
+                        float* dst = (col < N ? p.dB : p.dC) + (b * p.L + gt) * N + (col % N);
+                        red_add_v4(dst, acc01.x, acc01.y, acc23.x, acc23.y);
+                    }
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+    }
+
+#pragma unroll
+    for (int ch = 0; ch < 2; ++ch) {
+        if (!(ch ? dv1 : dv0)) continue;
+        const int64_t d = dch0 + ch * NPR;
+        if (p.gstate_out) {
+            // (a_0 gh_0, gv_0) = (lam, gv) after the first step
+            float* o = p.gstate_out + (rg.rec + ch * NPR) * (2 * N) + ng * NP;
+            st_pairs_g<NP>(o, lam[ch]);
+            st_pairs_g<NP>(o + N, gv[ch]);
+        }
+        float* dst = p.dA + d * N + ng * NP;
+#pragma unroll
+        for (int j = 0; j < NP2; ++j) {
+            atomicAdd(dst + 2 * j, dA[ch][j].x);
+            atomicAdd(dst + 2 * j + 1, dA[ch][j].y);
+        }
+    }
+    // dD, dbias: sum the pair's lanes
+    accD0 = lane_sum<0, LG>(accD0);
+    accD1 = lane_sum<0, LG>(accD1);
+    accB0 = lane_sum<0, LG>(accB0);
+    accB1 = lane_sum<0, LG>(accB1);
+    if (ng == 0) {
+        if (dv0) {
+            if (p.dD) atomicAdd(p.dD + dch0, accD0);
+            if (p.ddbias) atomicAdd(p.ddbias + dch0, accB0);
+        }
+        if (dv1) {
+            if (p.dD) atomicAdd(p.dD + dch0 + NPR, accD1);
+            if (p.ddbias) atomicAdd(p.ddbias + dch0 + NPR, accB1);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------
 // backward segment summary: the adjoint pair leaving the first step when none
 // arrives from after the last one, (lam^0, mu^0) = (a_0 gh_0, gv_0).  Needs
 // only delta (for a), z and dout (for dy) and C; a reverse sweep without the
@@ -1218,9 +1618,9 @@ __global__ void __launch_bounds__(MM_NT)
 // Tensor maps of the activation and B/C tiles a launch stages; false (and the
 // kernel falls back to cp.async) when the rows are not 16-byte aligned or the
 // driver declines an encoding.
-template <int N, int NP, class E, int NT = MM_NT, int TS = MM_T>
+template <int N, int NP, class E, int NT = MM_NT, int TS = MM_T, int DP = 1>
 bool mm_build_tmaps(const MMParams& p, MMTmaps& tm) {
-    using Cf = MMCfg<N, NP, NT, TS>;
+    using Cf = MMCfg<N, NP, NT, TS, DP>;
     if (!p.vec) return false;
     const int eb = E::BYTES;
     const int swz = eb == 4 ? Cf::SWB : 0;  // bf16 raw tiles land unswizzled
@@ -1244,10 +1644,10 @@ bool mm_build_tmaps(const MMParams& p, MMTmaps& tm) {
     return true;
 }
 
-template <int N, int NP, class E, int NT = MM_NT, int TS = MM_T>
+template <int N, int NP, class E, int NT = MM_NT, int TS = MM_T, int DP = 1>
 MMParams mm_launch_params(const MMParams& p0, MMTmaps& tm) {
     MMParams p = p0;
-    p.tma = mm_build_tmaps<N, NP, E, NT, TS>(p, tm) ? 1 : 0;
+    p.tma = mm_build_tmaps<N, NP, E, NT, TS, DP>(p, tm) ? 1 : 0;
     p.err = mmb_device_error_flag();
     return p;
 }
@@ -1304,8 +1704,34 @@ int launch_fwd_t(const MMParams& p0, cudaStream_t stream) {
 #ifndef MMB_BWD_T
 #define MMB_BWD_T MM_T
 #endif
+// The two-channel backward (mmscan_bwd2_kernel) for NP = 4 one-warp CTAs at
+// N = 8 / 16 / 32; MMB_BWD_DP2 = 0 keeps the one-channel kernel.  Its staged
+// chunks are MMB_BWD2_T steps (16: two stages of 6 KB plus the 8 KB window
+// buffer keep eight CTAs per SM within the shared memory).
+#ifndef MMB_BWD_DP2
+#define MMB_BWD_DP2 1
+#endif
+#ifndef MMB_BWD2_T
+#define MMB_BWD2_T 16
+#endif
+template <int N, bool SP, bool Z, class E>
+int launch_bwd2_t(const MMParams& p0, cudaStream_t stream);
+
+// The two-channel backward halves the CTAs of a call: it is picked when its grid
+// still gives every SM MM_BWD2_MIN_CTAS_PER_SM CTAs (per call, us: 939 -> 795 at
+// B=256 L=300 D=512, 817 -> 769 at B=128 L=1024 D=256, 188 -> 172 at B=2
+// L=8192 D=256 in 32 time chunks; at B=32 L=1024 D=256, 3.5 CTAs per SM, 238 ->
+// 298, so that call keeps the one-channel kernel).
+constexpr int MM_BWD2_MIN_CTAS_PER_SM = 6;
+
 template <int N, int NP, bool SP, bool Z, class E>
 int launch_bwd_t(const MMParams& p0, cudaStream_t stream) {
+    if constexpr (MMB_BWD_DP2 && MMB_BWD_NT == 32 && NP == 4 && N >= 8 && N <= 32) {
+        constexpr int DT2 = MMCfg<N, 4, 32, MMB_BWD2_T, 2>::DT;
+        const int64_t ctas = (p0.D + DT2 - 1) / DT2 * p0.Bsz * p0.nz;
+        if (ctas >= (int64_t)MM_SMS * MM_BWD2_MIN_CTAS_PER_SM)
+            return launch_bwd2_t<N, SP, Z, E>(p0, stream);
+    }
     // 32 threads only where a CTA keeps at least 8 channels (32-byte tile rows)
     constexpr int NT = (MMB_BWD_NT == 32 && 32 / (N / NP) >= 8) ? 32 : MM_NT;
     // steps per staged chunk: one-warp CTAs stage MMB_BWD_T
@@ -1323,6 +1749,23 @@ int launch_bwd_t(const MMParams& p0, cudaStream_t stream) {
     const MMParams p = mm_launch_params<N, NP, E, NT, TS>(p0, tm);
     dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz, (unsigned)p.nz);
     mmscan_bwd_kernel<N, NP, SP, Z, E, NT, TS><<<grid, NT, smem, stream>>>(p, tm);
+    return mmb_launch_status();
+}
+
+template <int N, bool SP, bool Z, class E>
+int launch_bwd2_t(const MMParams& p0, cudaStream_t stream) {
+    constexpr int NT = 32, TS = MMB_BWD2_T;
+    using Cf = MMCfg<N, 4, NT, TS, 2>;
+    const size_t smem = sizeof(float) * (MMSmem<N, 4, 4, E::BYTES, NT, TS, 2>::FLOATS +
+                                         MM_CK * (Cf::DT / 2) * 2 * N) +
+                        MM_SMEM_ALIGN;
+    static int attr_done[MMB_MAX_DEVICES] = {};
+    const int st = mmb_smem_attr(mmscan_bwd2_kernel<N, SP, Z, E, TS>, smem, attr_done);
+    if (st != MMB_OK) return st;
+    MMTmaps tm;
+    const MMParams p = mm_launch_params<N, 4, E, NT, TS, 2>(p0, tm);
+    dim3 grid((unsigned)((p.D + Cf::DT - 1) / Cf::DT), (unsigned)p.Bsz, (unsigned)p.nz);
+    mmscan_bwd2_kernel<N, SP, Z, E, TS><<<grid, NT, smem, stream>>>(p, tm);
     return mmb_launch_status();
 }
 
