@@ -70,7 +70,8 @@ def _bwd_kernels(Bsz, L, Dm, N):
     C = torch.randn(Bsz, L, N, device=dev, generator=g)
     y = selective_scan_momentum_fn(x, delta, A, B, C, None)
     torch.cuda.synchronize()
-    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+    with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA],
+                                acc_events=True) as prof:
         y.backward(torch.ones_like(y))
         torch.cuda.synchronize()
     return [e.name for e in prof.events() if "mmscan_bwd" in e.name]

@@ -126,17 +126,18 @@ def test_segments_reproduce_the_whole_sequence(dtype, Bsz, Dm, N, seg_lens, gate
 
 @pytest.mark.parametrize("L", [45, 64, 1])
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-def test_summaries_and_state_outputs(L, dtype):
+@pytest.mark.parametrize("Bsz,Dm", [(2, 64), (64, 256)])  # one- and two-channel kernels
+def test_summaries_and_state_outputs(L, dtype, Bsz, Dm):
     """Summaries, state_out and gstate_out of one segment, including a ragged
     length whose last 8-step block runs past the end."""
-    t = to_dev(make(7, 2, L, 64, 16), dtype)
+    t = to_dev(make(7, Bsz, L, Dm, 16), dtype)
     r = rounded(t)
     c = call_for(t, 0, L)
     summ = c.fwd_summary()
     so = oracle.mmscan_fwd_summary(r["x"], r["delta"], r["A"], r["B"], r["bias"], True, BETA, ALPHA)
     assert rel(summ, so) <= TOL
     rng = np.random.default_rng(1)
-    s_in = torch.from_numpy(rng.standard_normal((2, 64, 2, 16))).float().to(DEV)
+    s_in = torch.from_numpy(rng.standard_normal((Bsz, Dm, 2, 16))).float().to(DEV)
     y, ck, s_out = c.forward(True, state_in=s_in, want_state=True)
     yo, s_outo = oracle.mmscan_fwd(r["x"], r["delta"], r["A"], r["B"], r["C"], r["D"], r["z"],
                                    r["bias"], True, BETA, ALPHA, state_in=s_in.double().cpu().numpy(),
@@ -148,7 +149,8 @@ def test_summaries_and_state_outputs(L, dtype):
                            True, BETA, ALPHA, r["dout"], return_gstate=True)[8]
     assert rel(gs, go) <= TOL
     # the full backward's outgoing pair, with and without an incoming one
-    g_in = torch.from_numpy(rng.standard_normal((2, 64, 2, 16))).float().to(DEV) if L % 8 == 0 else None
+    g_in = (torch.from_numpy(rng.standard_normal((Bsz, Dm, 2, 16))).float().to(DEV)
+            if L % 8 == 0 else None)
     res = c.backward(ck, t["dout"], gstate_in=g_in, want_gstate=True)
     ro = oracle.mmscan_bwd(r["x"], r["delta"], r["A"], r["B"], r["C"], r["D"], r["z"], r["bias"],
                            True, BETA, ALPHA, r["dout"], state_in=s_in.double().cpu().numpy(),
