@@ -23,7 +23,7 @@ def test_sequence_sharded_scan_over_nccl():
     n = torch.cuda.device_count()
     if n < 2:
         pytest.skip("needs two GPUs")
-    ranks = min(n, 4)
+    ranks = min(n, 8)
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run",
            "--nnodes=1", f"--nproc-per-node={ranks}", "--master-addr", "127.0.0.1",
            "--master-port", str(_free_port()), os.path.join(HERE, "seqshard_nccl_worker.py")]
