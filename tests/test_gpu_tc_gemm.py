@@ -175,3 +175,23 @@ def test_unaligned_c_takes_the_per_tile_kernel(b_mn):
     C2 = torch.zeros(M, N, device=DEV)
     gemm(Af.t().contiguous(), Bt, M, N, K, 1, 1, C=C2, accumulate=1, splits=3)
     assert rel(C2.cpu(), ref) <= TOL
+
+
+def test_col_dot_accumulates_into_unaligned_output():
+    """An output that is not 16-byte aligned takes scalar atomics; accumulate=1
+    adds to what is there."""
+    lib = _lib.load()
+    M, N = 4097, 132
+    g = torch.Generator(device=DEV).manual_seed(41)
+    X = torch.randn(M, N, device=DEV, generator=g)
+    Y = torch.randn(M, N, device=DEV, generator=g)
+    buf = torch.randn(N + 1, device=DEV, generator=g)
+    out = buf[1:]  # 4 bytes past a 16-byte boundary
+    assert out.data_ptr() % 16 == 4
+    before = out.clone()
+    P = _lib.ptr
+    _lib.check(lib.mmb_col_dot_f32(M, N, P(X), N, P(Y), N, P(out), 1, _lib.stream_of(X)),
+               "mmb_col_dot_f32")
+    torch.cuda.synchronize()
+    ref = before.double().cpu() + (X.double() * Y.double()).sum(0).cpu()
+    assert rel(out.cpu(), ref) <= TOL
