@@ -47,10 +47,18 @@ __device__ __forceinline__ void mvec(const Mat2& m, float& u, float& v) {
     v = nv;
 }
 
-// Host-side chunking: enough (b, chunk, p) threads to fill the GPU, chunks of at
-// least 16 steps.
+// Host-side chunking: MMB_S2_THREADS_PER_SM (b, chunk, p) threads per SM, chunks
+// of at least 16 steps.  1024 rather than the 2048 an SM can hold: the LinOSS
+// backward's final pass keeps 512 threads per SM resident, and with half as
+// many, twice as long chunks it runs in two waves instead of four, each thread
+// amortising its first window's load over 14 windows instead of 7 (B=16
+// L=4096 P=256: backward 165 -> 140 us per call, forward unchanged; 512
+// threads per SM made the forward passes slower).
+#ifndef MMB_S2_THREADS_PER_SM
+#define MMB_S2_THREADS_PER_SM 1024
+#endif
 static void s2_chunks(int64_t Bsz, int64_t L, int64_t P, int64_t& T, int64_t& C) {
-    const int64_t target = 148 * 2048;
+    const int64_t target = 148 * MMB_S2_THREADS_PER_SM;
     int64_t chains = Bsz * P;
     int64_t want = (target + chains - 1) / chains;
     int64_t maxc = (L + 15) / 16;
@@ -684,7 +692,10 @@ __global__ void __launch_bounds__(S2_NT) lin_bwd_carry(const LinParams q) {
 // thread reads back only what it copied: no block barrier).
 constexpr int LIN_BWD_SLOT = 2 * S2_CK * 2 + 4;  // floats per thread and buffer: Bu, dx2, ckpt
 constexpr size_t LIN_BWD_SMEM = sizeof(float) * 2 * LIN_BWD_SLOT * S2_NT;
-__global__ void __launch_bounds__(S2_NT, 2) lin_bwd_final(const LinParams q) {
+#ifndef MMB_LIN_BWD_MIN_CTAS
+#define MMB_LIN_BWD_MIN_CTAS 2
+#endif
+__global__ void __launch_bounds__(S2_NT, MMB_LIN_BWD_MIN_CTAS) lin_bwd_final(const LinParams q) {
     extern __shared__ float4 lin_sm4[];
     const int tid = threadIdx.x;
     const int64_t idx = (int64_t)blockIdx.x * S2_NT + tid;
@@ -730,13 +741,11 @@ __global__ void __launch_bounds__(S2_NT, 2) lin_bwd_final(const LinParams q) {
             else
                 cp_async_commit();  // an empty group keeps the wait count uniform
             cp_async_wait<1>();
-            float2 us[S2_CK], gs[S2_CK];
-#pragma unroll
-            for (int s = 0; s < S2_CK; ++s) {
-                const bool in = ws + s < t1;
-                us[s] = in ? *slot2(buf, 0, s) : make_float2(0.f, 0.f);
-                gs[s] = in ? *slot2(buf, 1, s) : make_float2(0.f, 0.f);
-            }
+            // Bu and dx2 are read from this thread's slots where each step uses
+            // them (not held as register copies of the window: that pushed the
+            // kernel past its 128-register cap into local-memory spills).
+            // Steps past t1 replay with step ws's Bu; only the states they
+            // produce use it, and the adjoint skips those steps.
             const float4 x0 = smck[buf * S2_NT + tid];
             float xs[S2_CK + 1][4];
             xs[0][0] = x0.x; xs[0][1] = x0.y; xs[0][2] = x0.z; xs[0][3] = x0.w;
@@ -744,20 +753,22 @@ __global__ void __launch_bounds__(S2_NT, 2) lin_bwd_final(const LinParams q) {
             for (int s = 0; s < S2_CK; ++s) {
                 xs[s + 1][0] = xs[s][0]; xs[s + 1][1] = xs[s][1];
                 xs[s + 1][2] = xs[s][2]; xs[s + 1][3] = xs[s][3];
-                lin_step(k, us[s], xs[s + 1][0], xs[s + 1][1], xs[s + 1][2], xs[s + 1][3]);
+                lin_step(k, *slot2(buf, 0, s), xs[s + 1][0], xs[s + 1][1], xs[s + 1][2],
+                         xs[s + 1][3]);
             }
 #pragma unroll
             for (int s = S2_CK - 1; s >= 0; --s) {
                 if (ws + s >= t1) continue;
-                const float a1r = l1r, a1i = l1i, a2r = l2r + gs[s].x, a2i = l2i + gs[s].y;
+                const float2 us = *slot2(buf, 0, s), gs = *slot2(buf, 1, s);
+                const float a1r = l1r, a1i = l1i, a2r = l2r + gs.x, a2i = l2i + gs.y;
                 dbu[(ws + s) * q.P] = make_float2(k.f1 * a1r + k.f2 * a2r, k.f1 * a1i + k.f2 * a2i);
                 // state before step t (zero at t = 0: the checkpoint there is zero)
                 g[0] += a1r * xs[s][0] + a1i * xs[s][1];
                 g[1] += a1r * xs[s][2] + a1i * xs[s][3];
                 g[2] += a2r * xs[s][0] + a2i * xs[s][1];
                 g[3] += a2r * xs[s][2] + a2i * xs[s][3];
-                g[4] += a1r * us[s].x + a1i * us[s].y;
-                g[5] += a2r * us[s].x + a2i * us[s].y;
+                g[4] += a1r * us.x + a1i * us.y;
+                g[5] += a2r * us.x + a2i * us.y;
                 l1r = a1r; l1i = a1i; l2r = a2r; l2i = a2i;
                 mvec(mt, l1r, l2r);
                 mvec(mt, l1i, l2i);
