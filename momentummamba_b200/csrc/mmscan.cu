@@ -87,6 +87,12 @@ static double pow_int(double base, int64_t e) {
 
 // Incoming (h, v) of every chunk: zeros for chunk 0, then the fold of the
 // earlier chunks' summaries [h^0 | v^0 | P | Q'].  One thread per (b, d, n).
+// Both folds read each chunk's summary independently of the carried pair, so a
+// thread loads MM_CARRY_U chunks' summaries before folding them (one global
+// round trip per MM_CARRY_U chunks instead of one per chunk: 17-18 -> 8.4 us
+// per launch for 32 chunks at B=2 D=256 N=16).
+constexpr int MM_CARRY_U = 8;
+
 __global__ void chunk_carry_fwd_kernel(int64_t BD, int N, int nch, float beta, float betaTc,
                                        const float* __restrict__ summ,
                                        float* __restrict__ state_in) {
@@ -95,15 +101,32 @@ __global__ void chunk_carry_fwd_kernel(int64_t BD, int N, int nch, float beta, f
          e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t bd = e / N, n = e % N;
         float h = 0.f, v = 0.f;
-        for (int c = 0; c < nch; ++c) {
-            float* o = state_in + ((int64_t)c * BD + bd) * 2 * N;
-            o[n] = h;
-            o[N + n] = v;
-            if (c + 1 == nch) break;
-            const float* sm = summ + ((int64_t)c * BD + bd) * 4 * N;
-            const float hn = fmaf(sm[2 * N + n], h, fmaf(beta * sm[3 * N + n], v, sm[n]));
-            v = fmaf(betaTc, v, sm[N + n]);
-            h = hn;
+        for (int c0 = 0; c0 < nch; c0 += MM_CARRY_U) {
+            float h0[MM_CARRY_U], v0[MM_CARRY_U], P[MM_CARRY_U], Q[MM_CARRY_U];
+#pragma unroll
+            for (int u = 0; u < MM_CARRY_U; ++u) {
+                const int c = c0 + u;
+                h0[u] = v0[u] = P[u] = Q[u] = 0.f;
+                if (c + 1 < nch) {  // the last chunk's summary is not needed
+                    const float* sm = summ + ((int64_t)c * BD + bd) * 4 * N + n;
+                    h0[u] = sm[0];
+                    v0[u] = sm[N];
+                    P[u] = sm[2 * N];
+                    Q[u] = sm[3 * N];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < MM_CARRY_U; ++u) {
+                const int c = c0 + u;
+                if (c < nch) {
+                    float* o = state_in + ((int64_t)c * BD + bd) * 2 * N;
+                    o[n] = h;
+                    o[N + n] = v;
+                    const float hn = fmaf(P[u], h, fmaf(beta * Q[u], v, h0[u]));
+                    v = fmaf(betaTc, v, v0[u]);
+                    h = hn;
+                }
+            }
         }
     }
 }
@@ -118,18 +141,32 @@ __global__ void chunk_carry_bwd_kernel(int64_t BD, int N, int nch, float betaTc,
          e += (int64_t)gridDim.x * blockDim.x) {
         const int64_t bd = e / N, n = e % N;
         float lam = 0.f, mu = 0.f;
-        for (int c = nch - 1; c >= 0; --c) {
-            float* o = gstate_in + ((int64_t)c * BD + bd) * 2 * N;
-            o[n] = lam;
-            o[N + n] = mu;
-            if (c == 0) break;
-            const float* g = gsumm + ((int64_t)c * BD + bd) * 4 * N;
-            if (c == nch - 1) {  // nothing arrives after the last chunk
-                lam = g[n];
-                mu = g[N + n];
-            } else {
-                mu = fmaf(g[3 * N + n], lam, fmaf(betaTc, mu, g[N + n]));
-                lam = fmaf(g[2 * N + n], lam, g[n]);
+        for (int c0 = nch - 1; c0 >= 0; c0 -= MM_CARRY_U) {
+            float l0[MM_CARRY_U], m0[MM_CARRY_U], P[MM_CARRY_U], Q[MM_CARRY_U];
+#pragma unroll
+            for (int u = 0; u < MM_CARRY_U; ++u) {
+                const int c = c0 - u;
+                l0[u] = m0[u] = P[u] = Q[u] = 0.f;
+                if (c > 0) {  // the first chunk's summary is not needed
+                    const float* g = gsumm + ((int64_t)c * BD + bd) * 4 * N + n;
+                    l0[u] = g[0];
+                    m0[u] = g[N];
+                    P[u] = g[2 * N];
+                    Q[u] = g[3 * N];
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < MM_CARRY_U; ++u) {
+                const int c = c0 - u;
+                if (c >= 0) {
+                    float* o = gstate_in + ((int64_t)c * BD + bd) * 2 * N;
+                    o[n] = lam;
+                    o[N + n] = mu;
+                    // nothing arrives after the last chunk: (lam, mu) are zero
+                    // there, so the general fold gives (lam^0, mu^0)
+                    mu = fmaf(Q[u], lam, fmaf(betaTc, mu, m0[u]));
+                    lam = fmaf(P[u], lam, l0[u]);
+                }
             }
         }
     }
